@@ -1,0 +1,204 @@
+/*
+ * moe_b200.h - C ABI of the B200 (sm_100a) mixture-of-experts MLP hot path.
+ *
+ * Every entry point replaces one function of the reference Python/Triton
+ * package triton_moe (file:line given beside each declaration).  The ABI uses
+ * only plain pointers, sizes and a CUDA stream:
+ *   - all tensor pointers are DEVICE pointers, row-major, with the given row
+ *     stride in elements;
+ *   - integer metadata is int32 on the device;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     asynchronous on it and never synchronises the host;
+ *   - `status` (nullable) is a device int that kernels set to a negative
+ *     MOE_ERR_* code when they detect an error on the device (bad expert id,
+ *     capacity overflow, a bounded wait that gave up);
+ *   - return value: MOE_OK, or a negative MOE_ERR_* code for a host-side
+ *     argument or launch error.
+ * dtype codes: MOE_DTYPE_BF16 / MOE_DTYPE_F16 for the GEMMs; the permutation
+ * kernels also take MOE_DTYPE_F32.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_OK 0
+#define MOE_ERR_BAD_ARG (-1)
+#define MOE_ERR_UNSUPPORTED (-2)
+#define MOE_ERR_CUDA (-3)
+#define MOE_ERR_TIMEOUT (-4)
+#define MOE_ERR_CAPACITY (-5)
+#define MOE_ERR_BAD_EXPERT (-6)
+
+#define MOE_DTYPE_BF16 0
+#define MOE_DTYPE_F16 1
+#define MOE_DTYPE_F32 2
+
+#define MOE_ACT_NONE 0
+#define MOE_ACT_RELU_SQUARED 1
+
+#define MOE_ROUND_UP 0
+#define MOE_ROUND_DOWN 1
+#define MOE_ROUND_NEAREST 2
+
+/* Library identification and error text. */
+MOE_API const char* moe_version(void);
+MOE_API const char* moe_status_string(int status);
+
+/* Bytes of device workspace moe_route needs for `num_assignments` top-k
+ * assignments over `num_experts` experts. */
+MOE_API int64_t moe_route_workspace_bytes(int64_t num_assignments, int num_experts);
+
+/*
+ * Routing.  Replaces fused_route (triton_moe/kernels/fused_cumsum.py:84-171):
+ * stable sort of the flattened top-k expert ids, per-expert histogram,
+ * rounded inclusive cumsums (_cumsum_kernel, fused_cumsum.py:20-81) and the
+ * drop compaction of the "down"/"nearest" modes (fused_cumsum.py:154-169).
+ * Also produces the module's offsets (triton_moe/moe.py:192-202) and the
+ * padded-row maps used by the gather/scatter/GEMM kernels.
+ *   selected_experts   [num_assignments] int32 (selected_is_int64 = 0) or int64
+ *   bin_ids, indices   [num_assignments] (first bins[E-1] entries valid)
+ *   tokens_per_expert, bins, padded_bins, padded_tokens_per_expert  [E]
+ *   expert_token_offsets [E+1] = [0, padded_bins...]
+ *   row_to_assignment  [padded_capacity] or NULL: padded row -> assignment
+ *                      index (token*top_k + slot), -1 for padding rows
+ *   assignment_to_row  [num_assignments] or NULL: inverse map, -1 if dropped
+ *   workspace          moe_route_workspace_bytes(...) bytes of device memory
+ */
+MOE_API int moe_route(const void* selected_experts, int selected_is_int64, int64_t num_assignments,
+              int num_experts, int block_size, int rounding, int32_t* bin_ids, int32_t* indices,
+              int32_t* tokens_per_expert, int32_t* bins, int32_t* padded_bins,
+              int32_t* expert_token_offsets, int32_t* padded_tokens_per_expert,
+              int32_t* row_to_assignment, int64_t padded_capacity, int32_t* assignment_to_row,
+              void* workspace, int64_t workspace_bytes, int* status, void* stream);
+
+/*
+ * Padded-row maps from the reference's sorted-order metadata (indices,
+ * bin_ids, bins, padded_bins as returned by fused_route).  The row arithmetic
+ * is that of _padded_gather_kernel (triton_moe/kernels/gather.py:29-50).
+ * Either output may be NULL.
+ */
+MOE_API int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,
+                      const int32_t* padded_bins, int64_t num_kept, int64_t padded_rows,
+                      int32_t* row_to_assignment, int64_t num_assignments,
+                      int32_t* assignment_to_row, int* status, void* stream);
+
+/* precompute_gather_map (triton_moe/kernels/grouped_gemm.py:104-149):
+ * gather_map[r] = row_to_assignment[r] / top_k, padding rows 0. */
+MOE_API int moe_gather_map(const int32_t* row_to_assignment, int64_t padded_rows, int top_k,
+                   int32_t* gather_map, void* stream);
+
+/*
+ * Padded gather.  out[r] = x[row_map[r] / map_div] (* weights[row_map[r]] when
+ * weights != NULL); rows with a negative map entry are written as zeros.
+ * Rows r >= *padded_rows_device (when non-NULL) are left untouched.
+ * Replaces padded_gather (triton_moe/kernels/gather.py:63-116, map_div =
+ * top_k), _weighted_padded_gather (gather.py:177-218) and the fused-gather
+ * row indirection of the GEMMs (grouped_gemm.py:270-273, map_div = 1).
+ */
+MOE_API int moe_padded_gather(const void* x, int64_t ld_x, int64_t hidden, const int32_t* row_map,
+                      int map_div, int64_t padded_rows, const int32_t* padded_rows_device,
+                      const void* weights, void* out, int64_t ld_out, int dtype, void* stream);
+
+/*
+ * Weighted top-k combine.  out[t] = sum_j round(y[assignment_to_row[t*k+j]] *
+ * weights[t*k+j]); weights == NULL means unit weights.  Replaces
+ * padded_scatter (triton_moe/kernels/scatter.py:72-135) without the
+ * [T, k, H] temporary.
+ */
+MOE_API int moe_padded_scatter(const void* y, int64_t ld_y, int64_t hidden,
+                       const int32_t* assignment_to_row, int64_t num_tokens, int top_k,
+                       const void* weights, void* out, int64_t ld_out, int dtype, void* stream);
+
+/* relu^2 derivative: grad_act = pre > 0 ? grad_out * 2 * pre : 0, rounded to
+ * dtype (triton_moe/kernels/grouped_gemm.py:751-766). */
+MOE_API int moe_relu_squared_grad(const void* grad_out, const void* pre_act, int64_t rows, int64_t cols,
+                          int64_t ld, void* grad_act, int dtype, void* stream);
+
+/*
+ * Grouped GEMMs.  Common arguments:
+ *   expert_token_offsets  [E+1] row offsets of each expert's (padded) rows
+ *   expert_weight_offsets [E+1] offsets of each expert's columns of w1 /
+ *                         rows of w2
+ *   tokens_per_expert     [E] or NULL: caps the rows computed per expert
+ *   hidden                hidden size H; w1 is [H, total_width], w2 is
+ *                         [total_width, H], both contiguous
+ *   rows                  rows of the token-space operands (allocation size)
+ *   tile_n                128 or 256 (0 = choose)
+ * Every expert width and every expert row count used as a reduction length
+ * must be a multiple of 16; H must be a multiple of 16.
+ */
+
+/* grouped_gemm_up (triton_moe/kernels/grouped_gemm.py:378-477, kernel :212-368):
+ * out = act(x @ w1_e); with MOE_ACT_RELU_SQUARED and pre_act != NULL also
+ * pre_act = relu(x @ w1_e).  Columns >= w_e of out / pre_act are not written. */
+MOE_API int moe_grouped_gemm_up(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                        int64_t hidden, int64_t total_width,
+                        const int32_t* expert_token_offsets,
+                        const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert,
+                        int num_experts, int activation, void* out, void* pre_act,
+                        int64_t ld_out, int dtype, int tile_n, int* status, void* stream);
+
+/* grouped_gemm_down (grouped_gemm.py:586-651, kernel :480-583):
+ * out[rows_e] = inter[rows_e, :w_e] @ w2[w_e rows]. */
+MOE_API int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
+                          int64_t hidden, int64_t total_width,
+                          const int32_t* expert_token_offsets,
+                          const int32_t* expert_weight_offsets,
+                          const int32_t* tokens_per_expert, int num_experts, void* out,
+                          int64_t ld_out, int dtype, int tile_n, int* status, void* stream);
+
+/* dX half of grouped_gemm_up_backward (grouped_gemm.py:1165-1290, kernel
+ * :654-802) with the activation derivative already applied:
+ * grad_x[rows_e] = grad_act[rows_e, :w_e] @ w1_e^T. */
+MOE_API int moe_grouped_gemm_up_dx(const void* grad_act, int64_t rows, int64_t ld_grad_act,
+                           const void* w1, int64_t hidden, int64_t total_width,
+                           const int32_t* expert_token_offsets,
+                           const int32_t* expert_weight_offsets,
+                           const int32_t* tokens_per_expert, int num_experts, void* grad_x,
+                           int64_t ld_grad_x, int dtype, int tile_n, int* status, void* stream);
+
+/* dW half of grouped_gemm_up_backward (kernel grouped_gemm.py:805-967):
+ * grad_w1[:, w_e cols] = x[rows_e]^T @ grad_act[rows_e, :w_e], reduced over
+ * each expert's full row range (experts with no rows get zeros). */
+MOE_API int moe_grouped_gemm_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_act,
+                           int64_t ld_grad_act, int64_t hidden, int64_t total_width,
+                           const int32_t* expert_token_offsets,
+                           const int32_t* expert_weight_offsets, int num_experts,
+                           void* grad_w1, int dtype, int tile_n, int* status, void* stream);
+
+/* dIntermediate half of grouped_gemm_down_backward (grouped_gemm.py:1293-1390,
+ * kernel :970-1063): grad_inter[rows_e, :w_e] = grad_y[rows_e] @ w2_e^T.
+ * When pre_act != NULL the relu^2 derivative is fused into the epilogue and
+ * `out` receives grad_act = relu2'(pre_act) * round(grad_inter) instead. */
+MOE_API int moe_grouped_gemm_down_dinter(const void* grad_y, int64_t rows, int64_t ld_grad_y,
+                                 const void* w2, int64_t hidden, int64_t total_width,
+                                 const int32_t* expert_token_offsets,
+                                 const int32_t* expert_weight_offsets,
+                                 const int32_t* tokens_per_expert, int num_experts,
+                                 const void* pre_act, int64_t ld_pre, void* out, int64_t ld_out,
+                                 int dtype, int tile_n, int* status, void* stream);
+
+/* dW half of grouped_gemm_down_backward (kernel grouped_gemm.py:1066-1162):
+ * grad_w2[w_e rows] = inter[rows_e, :w_e]^T @ grad_y[rows_e]. */
+MOE_API int moe_grouped_gemm_down_dw(const void* inter, int64_t rows, int64_t ld_inter,
+                             const void* grad_y, int64_t ld_grad_y, int64_t hidden,
+                             int64_t total_width, const int32_t* expert_token_offsets,
+                             const int32_t* expert_weight_offsets, int num_experts,
+                             void* grad_w2, int dtype, int tile_n, int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

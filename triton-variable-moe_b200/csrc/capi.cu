@@ -1,0 +1,335 @@
+// extern "C" entry points of libmoe_b200 (declared in include/moe_b200.h).
+// Each one validates its host-side arguments, maps the reference operation
+// onto the kernels of route.cu / permute.cu / grouped_gemm.cu and launches on
+// the caller's stream.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/moe_b200.h"
+#include "grouped_gemm.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+long long route_workspace_bytes(long long A, int E);
+int route(const void* sel, int sel_is_int64, long long A, int E, int bs, int mode,
+          int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins, int32_t* padded_bins,
+          int32_t* tok_off, int32_t* ptpe, int32_t* row_asg, long long p_cap, int32_t* asg_row,
+          void* ws, long long ws_bytes, int* status, cudaStream_t st);
+int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
+                long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
+                int dtype, cudaStream_t st);
+int combine_rows(const void* y, long long ldy, int H, const int32_t* asg_row, long long T_tokens,
+                 int k, const void* w, void* out, long long ldo, int dtype, cudaStream_t st);
+int relu2_grad(const void* g, const void* pre, long long rows, long long cols, long long ld,
+               void* out, int dtype, cudaStream_t st);
+int build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,
+                  const int32_t* padded_bins, long long n_kept, long long p_rows,
+                  int32_t* row_asg, long long n_asg, int32_t* asg_row, int* status,
+                  cudaStream_t st);
+int gather_map_from_rows(const int32_t* row_asg, long long rows, int k, int32_t* gmap,
+                         cudaStream_t st);
+}  // namespace moe
+
+namespace {
+
+using moe::GemmOperands;
+using moe::GroupedGemmDesc;
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool gemm_dtype_ok(int dtype) { return dtype == MOE_DTYPE_BF16 || dtype == MOE_DTYPE_F16; }
+
+int pick_bn(int tile_n, long long n_hint) {
+  if (tile_n == 128 || tile_n == 256) return tile_n;
+  return (n_hint > 0 && n_hint % 256 == 0) ? 256 : 128;
+}
+
+GroupedGemmDesc base_desc(const int32_t* tok_off, const int32_t* tok_cnt, const int32_t* w_off,
+                          int E, long long hidden, int* status) {
+  GroupedGemmDesc g{};
+  g.tok_off = tok_off;
+  g.tok_cnt = tok_cnt;
+  g.w_off = w_off;
+  g.E = E;
+  g.cdim = static_cast<int>(hidden);
+  g.status = status;
+  return g;
+}
+
+bool common_ok(long long rows, long long hidden, long long total_width, const int32_t* tok_off,
+               const int32_t* w_off, int E) {
+  return rows >= 1 && hidden >= 16 && hidden % 16 == 0 && total_width >= 16 &&
+         total_width % 16 == 0 && tok_off && w_off && E >= 1 && E <= moe::kMaxGroups;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* moe_version(void) { return "moe_b200 0.1 (sm_100a tcgen05)"; }
+
+const char* moe_status_string(int s) {
+  switch (s) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_BAD_ARG: return "invalid argument";
+    case MOE_ERR_UNSUPPORTED: return "unsupported configuration";
+    case MOE_ERR_CUDA: return "CUDA error";
+    case MOE_ERR_TIMEOUT: return "device-side wait timed out";
+    case MOE_ERR_CAPACITY: return "padded row capacity exceeded";
+    case MOE_ERR_BAD_EXPERT: return "expert id out of range";
+    default: return "unknown status";
+  }
+}
+
+int64_t moe_route_workspace_bytes(int64_t num_assignments, int num_experts) {
+  if (num_assignments < 0 || num_experts <= 0) return 0;
+  return moe::route_workspace_bytes(num_assignments, num_experts);
+}
+
+int moe_route(const void* selected_experts, int selected_is_int64, int64_t num_assignments,
+              int num_experts, int block_size, int rounding, int32_t* bin_ids, int32_t* indices,
+              int32_t* tokens_per_expert, int32_t* bins, int32_t* padded_bins,
+              int32_t* expert_token_offsets, int32_t* padded_tokens_per_expert,
+              int32_t* row_to_assignment, int64_t padded_capacity, int32_t* assignment_to_row,
+              void* workspace, int64_t workspace_bytes, int* status, void* stream) {
+  return moe::route(selected_experts, selected_is_int64, num_assignments, num_experts,
+                    block_size, rounding, bin_ids, indices, tokens_per_expert, bins, padded_bins,
+                    expert_token_offsets, padded_tokens_per_expert, row_to_assignment,
+                    padded_capacity, assignment_to_row, workspace, workspace_bytes, status,
+                    S(stream));
+}
+
+int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,
+                      const int32_t* padded_bins, int64_t num_kept, int64_t padded_rows,
+                      int32_t* row_to_assignment, int64_t num_assignments,
+                      int32_t* assignment_to_row, int* status, void* stream) {
+  if (num_kept < 0 || padded_rows < 0 || num_assignments < 0) return MOE_ERR_BAD_ARG;
+  if (num_kept > 0 && (!indices || !bin_ids || !bins || !padded_bins)) return MOE_ERR_BAD_ARG;
+  return moe::build_row_map(indices, bin_ids, bins, padded_bins, num_kept, padded_rows,
+                            row_to_assignment, num_assignments, assignment_to_row, status,
+                            S(stream));
+}
+
+int moe_gather_map(const int32_t* row_to_assignment, int64_t padded_rows, int top_k,
+                   int32_t* gather_map, void* stream) {
+  if (top_k <= 0 || padded_rows < 0) return MOE_ERR_BAD_ARG;
+  return moe::gather_map_from_rows(row_to_assignment, padded_rows, top_k, gather_map, S(stream));
+}
+
+int moe_padded_gather(const void* x, int64_t ld_x, int64_t hidden, const int32_t* row_map,
+                      int map_div, int64_t padded_rows, const int32_t* padded_rows_device,
+                      const void* weights, void* out, int64_t ld_out, int dtype, void* stream) {
+  if (map_div <= 0 || hidden < 0 || padded_rows < 0 || ld_x < hidden || ld_out < hidden)
+    return MOE_ERR_BAD_ARG;
+  if (padded_rows > 0 && (!x || !row_map || !out)) return MOE_ERR_BAD_ARG;
+  return moe::gather_rows(x, ld_x, static_cast<int>(hidden), row_map, map_div, padded_rows,
+                          padded_rows_device, weights, out, ld_out, dtype, S(stream));
+}
+
+int moe_padded_scatter(const void* y, int64_t ld_y, int64_t hidden,
+                       const int32_t* assignment_to_row, int64_t num_tokens, int top_k,
+                       const void* weights, void* out, int64_t ld_out, int dtype, void* stream) {
+  if (top_k <= 0 || hidden < 0 || num_tokens < 0 || ld_y < hidden || ld_out < hidden)
+    return MOE_ERR_BAD_ARG;
+  if (num_tokens > 0 && (!y || !assignment_to_row || !out)) return MOE_ERR_BAD_ARG;
+  return moe::combine_rows(y, ld_y, static_cast<int>(hidden), assignment_to_row, num_tokens,
+                           top_k, weights, out, ld_out, dtype, S(stream));
+}
+
+int moe_relu_squared_grad(const void* grad_out, const void* pre_act, int64_t rows, int64_t cols,
+                          int64_t ld, void* grad_act, int dtype, void* stream) {
+  if (rows < 0 || cols < 0 || ld < cols) return MOE_ERR_BAD_ARG;
+  return moe::relu2_grad(grad_out, pre_act, rows, cols, ld, grad_act, dtype, S(stream));
+}
+
+int moe_grouped_gemm_up(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                        int64_t hidden, int64_t total_width,
+                        const int32_t* expert_token_offsets,
+                        const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert,
+                        int num_experts, int activation, void* out, void* pre_act,
+                        int64_t ld_out, int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !x || !w1 || !out || ld_x < hidden || ld_out < 16 || ld_out % 8 != 0)
+    return MOE_ERR_BAD_ARG;
+  if (activation != MOE_ACT_NONE && activation != MOE_ACT_RELU_SQUARED) return MOE_ERR_UNSUPPORTED;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_TOKENS;
+  g.n_src = moe::DIM_WIDTH;
+  g.k_src = moe::DIM_CONST;
+  g.a_m_base = moe::BASE_TOK;
+  g.a_k_base = moe::BASE_ZERO;
+  g.b_n_base = moe::BASE_WOFF;
+  g.b_k_base = moe::BASE_ZERO;
+  g.d_m_base = moe::BASE_TOK;
+  g.d_n_base = moe::BASE_ZERO;
+  g.d = out;
+  g.ldd = ld_out;
+  int epi = moe::EPI_STORE;
+  if (activation == MOE_ACT_RELU_SQUARED) {
+    epi = moe::EPI_RELU2;
+    // without a pre_act buffer the relu output is written to `out` first and
+    // then overwritten by its square (same element, same thread)
+    g.aux = pre_act ? pre_act : out;
+    g.ld_aux = ld_out;
+  }
+  GemmOperands op{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
+                  pick_bn(tile_n, 0), 0};
+  return moe::run_grouped_gemm(op, g, epi, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
+                          int64_t hidden, int64_t total_width,
+                          const int32_t* expert_token_offsets,
+                          const int32_t* expert_weight_offsets,
+                          const int32_t* tokens_per_expert, int num_experts, void* out,
+                          int64_t ld_out, int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !inter || !w2 || !out || ld_inter < 16 || ld_inter % 8 != 0 || ld_out < hidden)
+    return MOE_ERR_BAD_ARG;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_TOKENS;
+  g.n_src = moe::DIM_CONST;
+  g.k_src = moe::DIM_WIDTH;
+  g.a_m_base = moe::BASE_TOK;
+  g.a_k_base = moe::BASE_ZERO;
+  g.b_n_base = moe::BASE_ZERO;
+  g.b_k_base = moe::BASE_WOFF;
+  g.d_m_base = moe::BASE_TOK;
+  g.d_n_base = moe::BASE_ZERO;
+  g.d = out;
+  g.ldd = ld_out;
+  GemmOperands op{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
+                  pick_bn(tile_n, hidden), 0};
+  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int moe_grouped_gemm_up_dx(const void* grad_act, int64_t rows, int64_t ld_grad_act,
+                           const void* w1, int64_t hidden, int64_t total_width,
+                           const int32_t* expert_token_offsets,
+                           const int32_t* expert_weight_offsets,
+                           const int32_t* tokens_per_expert, int num_experts, void* grad_x,
+                           int64_t ld_grad_x, int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !grad_act || !w1 || !grad_x || ld_grad_act < 16 || ld_grad_act % 8 != 0 ||
+      ld_grad_x < hidden)
+    return MOE_ERR_BAD_ARG;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_TOKENS;
+  g.n_src = moe::DIM_CONST;
+  g.k_src = moe::DIM_WIDTH;
+  g.a_m_base = moe::BASE_TOK;
+  g.a_k_base = moe::BASE_ZERO;
+  g.b_n_base = moe::BASE_ZERO;
+  g.b_k_base = moe::BASE_WOFF;
+  g.d_m_base = moe::BASE_TOK;
+  g.d_n_base = moe::BASE_ZERO;
+  g.d = grad_x;
+  g.ldd = ld_grad_x;
+  // B = w1 read K-major: rows are the hidden (N) index, columns the width (K)
+  GemmOperands op{grad_act, rows, ld_grad_act, ld_grad_act, 0, w1, hidden, total_width,
+                  total_width, 0, pick_bn(tile_n, hidden), 0};
+  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int moe_grouped_gemm_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_act,
+                           int64_t ld_grad_act, int64_t hidden, int64_t total_width,
+                           const int32_t* expert_token_offsets,
+                           const int32_t* expert_weight_offsets, int num_experts,
+                           void* grad_w1, int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !x || !grad_act || !grad_w1 || ld_x < hidden || ld_grad_act < 16 || ld_grad_act % 8 != 0)
+    return MOE_ERR_BAD_ARG;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, nullptr, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_CONST;
+  g.n_src = moe::DIM_WIDTH;
+  g.k_src = moe::DIM_TOKENS;
+  g.a_m_base = moe::BASE_ZERO;
+  g.a_k_base = moe::BASE_TOK;
+  g.b_n_base = moe::BASE_ZERO;
+  g.b_k_base = moe::BASE_TOK;
+  g.d_m_base = moe::BASE_ZERO;
+  g.d_n_base = moe::BASE_WOFF;
+  g.d = grad_w1;
+  g.ldd = total_width;
+  GemmOperands op{x, rows, hidden, ld_x, 1, grad_act, rows, ld_grad_act, ld_grad_act, 1,
+                  pick_bn(tile_n, 0), 0};
+  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int moe_grouped_gemm_down_dinter(const void* grad_y, int64_t rows, int64_t ld_grad_y,
+                                 const void* w2, int64_t hidden, int64_t total_width,
+                                 const int32_t* expert_token_offsets,
+                                 const int32_t* expert_weight_offsets,
+                                 const int32_t* tokens_per_expert, int num_experts,
+                                 const void* pre_act, int64_t ld_pre, void* out, int64_t ld_out,
+                                 int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !grad_y || !w2 || !out || ld_grad_y < hidden || ld_out < 16 || ld_out % 8 != 0 ||
+      (pre_act && (ld_pre < 16 || ld_pre % 8 != 0)))
+    return MOE_ERR_BAD_ARG;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_TOKENS;
+  g.n_src = moe::DIM_WIDTH;
+  g.k_src = moe::DIM_CONST;
+  g.a_m_base = moe::BASE_TOK;
+  g.a_k_base = moe::BASE_ZERO;
+  g.b_n_base = moe::BASE_WOFF;
+  g.b_k_base = moe::BASE_ZERO;
+  g.d_m_base = moe::BASE_TOK;
+  g.d_n_base = moe::BASE_ZERO;
+  g.d = out;
+  g.ldd = ld_out;
+  g.aux = const_cast<void*>(pre_act);
+  g.ld_aux = ld_pre;
+  // B = w2 read K-major: rows are the width (N) index, columns the hidden (K)
+  GemmOperands op{grad_y, rows, hidden, ld_grad_y, 0, w2, total_width, hidden, hidden, 0,
+                  pick_bn(tile_n, 0), 0};
+  return moe::run_grouped_gemm(op, g, pre_act ? moe::EPI_DACT : moe::EPI_STORE,
+                               dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int moe_grouped_gemm_down_dw(const void* inter, int64_t rows, int64_t ld_inter,
+                             const void* grad_y, int64_t ld_grad_y, int64_t hidden,
+                             int64_t total_width, const int32_t* expert_token_offsets,
+                             const int32_t* expert_weight_offsets, int num_experts,
+                             void* grad_w2, int dtype, int tile_n, int* status, void* stream) {
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
+                 num_experts) ||
+      !inter || !grad_y || !grad_w2 || ld_inter < 16 || ld_inter % 8 != 0 || ld_grad_y < hidden)
+    return MOE_ERR_BAD_ARG;
+  GroupedGemmDesc g = base_desc(expert_token_offsets, nullptr, expert_weight_offsets,
+                                num_experts, hidden, status);
+  g.m_src = moe::DIM_WIDTH;
+  g.n_src = moe::DIM_CONST;
+  g.k_src = moe::DIM_TOKENS;
+  g.a_m_base = moe::BASE_ZERO;
+  g.a_k_base = moe::BASE_TOK;
+  g.b_n_base = moe::BASE_ZERO;
+  g.b_k_base = moe::BASE_TOK;
+  g.d_m_base = moe::BASE_WOFF;
+  g.d_n_base = moe::BASE_ZERO;
+  g.d = grad_w2;
+  g.ldd = hidden;
+  GemmOperands op{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_grad_y, 1,
+                  pick_bn(tile_n, hidden), 0};
+  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+}  // extern "C"

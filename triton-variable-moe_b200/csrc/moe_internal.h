@@ -1,0 +1,39 @@
+// Internal declarations shared by the .cu translation units of libmoe_b200.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace moe {
+
+// Status codes (mirrored by the MOE_* constants of the public header).
+constexpr int kStatusOk = 0;
+constexpr int kStatusBadArg = -1;
+constexpr int kStatusUnsupported = -2;
+constexpr int kStatusCuda = -3;
+constexpr int kStatusTimeout = -4;
+constexpr int kStatusCapacity = -5;
+constexpr int kStatusBadExpert = -6;
+
+struct GroupedGemmDesc;
+
+// Dense operand views for one grouped GEMM launch.  Both operands are
+// row-major [rows, cols] with a row stride in elements.  `a_mn` / `b_mn`
+// select the MN-major reading (rows are the reduction dimension).
+struct GemmOperands {
+  const void* a;
+  long long a_rows, a_cols, lda;
+  int a_mn;
+  const void* b;
+  long long b_rows, b_cols, ldb;
+  int b_mn;
+  int bn;    // N tile: 128 or 256
+  int grid;  // CTAs; 0 = one per SM
+};
+
+int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int is_f16,
+                     cudaStream_t st);
+
+int num_sms();
+
+}  // namespace moe

@@ -1,0 +1,327 @@
+// Token permutation kernels (HBM-bound): padded gather, weighted padded
+// gather, weighted top-k combine, relu^2 derivative, and the small index
+// kernels that convert between the reference's sorted-order metadata and the
+// padded-row maps the other kernels consume.
+//
+// Semantics follow triton_moe/kernels/gather.py:13-60,123-174 and
+// triton_moe/kernels/scatter.py:13-69,104-133: padding rows are zero, a
+// weighted row is round(x * w) in the storage dtype, and the combine sums the
+// rounded per-expert products of a token in fp32 and rounds once.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "moe_internal.h"
+
+namespace moe {
+namespace {
+
+template <typename T>
+struct V8;  // 8 elements <-> uint4
+template <>
+struct V8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const uint4& u, float (&f)[8]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  static __device__ __forceinline__ uint4 store(const float (&f)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+  }
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float rnd(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+};
+template <>
+struct V8<__half> {
+  static __device__ __forceinline__ void load(const uint4& u, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  static __device__ __forceinline__ uint4 store(const float (&f)[8]) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+  }
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ float rnd(float v) { return __half2float(__float2half_rn(v)); }
+};
+// fp32 storage (used by the fp32 module path: plain copies, no rounding)
+template <>
+struct V8<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+  static __device__ __forceinline__ float rnd(float v) { return v; }
+};
+
+constexpr int kRowsPerBlock = 8;  // one warp per row
+
+// out[r, :] = src row map[r] / div of x (times w[map[r]] when w != null);
+// rows whose map entry is negative are zero.  Rows at or beyond *rows_dev
+// (when given) are not touched.
+template <typename T, bool VEC>
+__global__ void gather_rows_kernel(const T* __restrict__ x, long long ldx, int H,
+                                   const int32_t* __restrict__ map, int div, long long rows,
+                                   const int32_t* __restrict__ rows_dev,
+                                   const T* __restrict__ w, T* __restrict__ out, long long ldo) {
+  const int lane = threadIdx.x & 31;
+  long long nrows = rows;
+  if (rows_dev != nullptr) nrows = min(nrows, static_cast<long long>(*rows_dev));
+  for (long long r = static_cast<long long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+       r < nrows; r += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
+    const int a = map[r];
+    T* orow = out + r * ldo;
+    if (a < 0) {
+      if constexpr (VEC) {
+        for (int c = lane * 8; c < H; c += 256) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+      } else {
+        for (int c = lane; c < H; c += 32) orow[c] = V8<T>::from_f(0.f);
+      }
+      continue;
+    }
+    const T* xrow = x + static_cast<long long>(a / div) * ldx;
+    if constexpr (VEC) {
+      if (w == nullptr) {
+        for (int c = lane * 8; c < H; c += 256)
+          *reinterpret_cast<uint4*>(orow + c) = __ldg(reinterpret_cast<const uint4*>(xrow + c));
+      } else {
+        const float s = V8<T>::to_f(w[a]);
+        for (int c = lane * 8; c < H; c += 256) {
+          float f[8];
+          V8<T>::load(__ldg(reinterpret_cast<const uint4*>(xrow + c)), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] *= s;
+          *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(f);
+        }
+      }
+    } else {
+      const float s = w ? V8<T>::to_f(w[a]) : 1.f;
+      for (int c = lane; c < H; c += 32)
+        orow[c] = w ? V8<T>::from_f(V8<T>::to_f(xrow[c]) * s) : xrow[c];
+    }
+  }
+}
+
+// out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding)
+template <typename T, bool VEC>
+__global__ void combine_kernel(const T* __restrict__ y, long long ldy, int H,
+                               const int32_t* __restrict__ asg_row, long long T_tokens, int k,
+                               const T* __restrict__ w, T* __restrict__ out, long long ldo) {
+  const int lane = threadIdx.x & 31;
+  for (long long t = static_cast<long long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+       t < T_tokens; t += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
+    const int32_t* rows = asg_row + t * k;
+    T* orow = out + t * ldo;
+    if constexpr (VEC) {
+      for (int c = lane * 8; c < H; c += 256) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < k; ++j) {
+          const int row = rows[j];
+          if (row < 0) continue;
+          float f[8];
+          V8<T>::load(__ldg(reinterpret_cast<const uint4*>(y + row * ldy + c)), f);
+          if (w != nullptr) {
+            const float s = V8<T>::to_f(w[t * k + j]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += V8<T>::rnd(f[i] * s);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += f[i];
+          }
+        }
+        *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(acc);
+      }
+    } else {
+      for (int c = lane; c < H; c += 32) {
+        float acc = 0.f;
+        for (int j = 0; j < k; ++j) {
+          const int row = rows[j];
+          if (row < 0) continue;
+          const float v = V8<T>::to_f(y[row * ldy + c]);
+          acc += w ? V8<T>::rnd(v * V8<T>::to_f(w[t * k + j])) : v;
+        }
+        orow[c] = V8<T>::from_f(acc);
+      }
+    }
+  }
+}
+
+// grad_act = pre > 0 ? round(g * 2 * pre) : 0, elementwise over [rows, cols].
+template <typename T>
+__global__ void relu2_grad_kernel(const T* __restrict__ g, const T* __restrict__ pre,
+                                  long long rows, long long cols, long long ld,
+                                  T* __restrict__ out) {
+  const long long n = rows * cols;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols, c = i % cols;
+    const float p = V8<T>::to_f(pre[r * ld + c]);
+    const float gv = V8<T>::to_f(g[r * ld + c]);
+    out[r * ld + c] = V8<T>::from_f(p > 0.f ? gv * 2.0f * p : 0.f);
+  }
+}
+
+// Sorted-order metadata -> padded row maps (row_asg pre-filled with -1).
+__global__ void build_row_map_kernel(const int32_t* __restrict__ indices,
+                                     const int32_t* __restrict__ bin_ids,
+                                     const int32_t* __restrict__ bins,
+                                     const int32_t* __restrict__ padded_bins, long long n_kept,
+                                     long long p_rows, int32_t* __restrict__ row_asg,
+                                     int32_t* __restrict__ asg_row, int* status) {
+  for (long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; p < n_kept;
+       p += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int e = bin_ids[p];
+    const long long bstart = e > 0 ? bins[e - 1] : 0;
+    const long long pstart = e > 0 ? padded_bins[e - 1] : 0;
+    const long long row = pstart + (p - bstart);
+    const int a = indices[p];
+    if (row < 0 || row >= p_rows) {
+      if (status) atomicExch(status, kStatusCapacity);
+      continue;
+    }
+    if (row_asg) row_asg[row] = a;
+    if (asg_row) asg_row[a] = static_cast<int32_t>(row);
+  }
+}
+
+// precompute_gather_map's format: padded row -> source token, padding rows 0.
+__global__ void gather_map_kernel(const int32_t* __restrict__ row_asg, long long rows, int k,
+                                  int32_t* __restrict__ gmap) {
+  for (long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows;
+       r += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int a = row_asg[r];
+    gmap[r] = a >= 0 ? a / k : 0;
+  }
+}
+
+int grid_for(long long work_items, int per_block) {
+  long long b = (work_items + per_block - 1) / per_block;
+  const long long cap = static_cast<long long>(num_sms()) * 16;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return static_cast<int>(b);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename T>
+int gather_t(const void* x, long long ldx, int H, const int32_t* map, int div, long long rows,
+             const int32_t* rows_dev, const void* w, void* out, long long ldo, cudaStream_t st) {
+  if (rows <= 0) return kStatusOk;
+  const int grid = grid_for(rows, kRowsPerBlock);
+  const bool vec = H % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && aligned16(x) && aligned16(out);
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      gather_rows_kernel<T, true><<<grid, kRowsPerBlock * 32, 0, st>>>(
+          static_cast<const T*>(x), ldx, H, map, div, rows, rows_dev, static_cast<const T*>(w),
+          static_cast<T*>(out), ldo);
+      return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+    }
+  }
+  gather_rows_kernel<T, false><<<grid, kRowsPerBlock * 32, 0, st>>>(
+        static_cast<const T*>(x), ldx, H, map, div, rows, rows_dev, static_cast<const T*>(w),
+        static_cast<T*>(out), ldo);
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+template <typename T>
+int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long long T_tokens,
+              int k, const void* w, void* out, long long ldo, cudaStream_t st) {
+  if (T_tokens <= 0) return kStatusOk;
+  const int grid = grid_for(T_tokens, kRowsPerBlock);
+  const bool vec = H % 8 == 0 && ldy % 8 == 0 && ldo % 8 == 0 && aligned16(y) && aligned16(out);
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      combine_kernel<T, true><<<grid, kRowsPerBlock * 32, 0, st>>>(
+          static_cast<const T*>(y), ldy, H, asg_row, T_tokens, k, static_cast<const T*>(w),
+          static_cast<T*>(out), ldo);
+      return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+    }
+  }
+  combine_kernel<T, false><<<grid, kRowsPerBlock * 32, 0, st>>>(
+        static_cast<const T*>(y), ldy, H, asg_row, T_tokens, k, static_cast<const T*>(w),
+        static_cast<T*>(out), ldo);
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+}  // namespace
+
+// dtype: 0 bf16, 1 fp16, 2 fp32
+int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
+                long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
+                int dtype, cudaStream_t st) {
+  if (dtype == 0) return gather_t<__nv_bfloat16>(x, ldx, H, map, div, rows, rows_dev, w, out, ldo, st);
+  if (dtype == 1) return gather_t<__half>(x, ldx, H, map, div, rows, rows_dev, w, out, ldo, st);
+  if (dtype == 2) return gather_t<float>(x, ldx, H, map, div, rows, rows_dev, w, out, ldo, st);
+  return kStatusUnsupported;
+}
+
+int combine_rows(const void* y, long long ldy, int H, const int32_t* asg_row, long long T_tokens,
+                 int k, const void* w, void* out, long long ldo, int dtype, cudaStream_t st) {
+  if (dtype == 0) return combine_t<__nv_bfloat16>(y, ldy, H, asg_row, T_tokens, k, w, out, ldo, st);
+  if (dtype == 1) return combine_t<__half>(y, ldy, H, asg_row, T_tokens, k, w, out, ldo, st);
+  if (dtype == 2) return combine_t<float>(y, ldy, H, asg_row, T_tokens, k, w, out, ldo, st);
+  return kStatusUnsupported;
+}
+
+int relu2_grad(const void* g, const void* pre, long long rows, long long cols, long long ld,
+               void* out, int dtype, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return kStatusOk;
+  const int grid = grid_for(rows * cols, 256);
+  if (dtype == 0)
+    relu2_grad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(pre), rows, cols,
+        ld, static_cast<__nv_bfloat16*>(out));
+  else if (dtype == 1)
+    relu2_grad_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(g),
+                                                    static_cast<const __half*>(pre), rows, cols,
+                                                    ld, static_cast<__half*>(out));
+  else if (dtype == 2)
+    relu2_grad_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(g),
+                                                   static_cast<const float*>(pre), rows, cols, ld,
+                                                   static_cast<float*>(out));
+  else
+    return kStatusUnsupported;
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+int build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,
+                  const int32_t* padded_bins, long long n_kept, long long p_rows,
+                  int32_t* row_asg, long long n_asg, int32_t* asg_row, int* status,
+                  cudaStream_t st) {
+  if (row_asg && p_rows > 0) cudaMemsetAsync(row_asg, 0xFF, p_rows * 4, st);
+  if (asg_row && n_asg > 0) cudaMemsetAsync(asg_row, 0xFF, n_asg * 4, st);
+  if (n_kept > 0)
+    build_row_map_kernel<<<grid_for(n_kept, 256), 256, 0, st>>>(
+        indices, bin_ids, bins, padded_bins, n_kept, p_rows, row_asg, asg_row, status);
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+int gather_map_from_rows(const int32_t* row_asg, long long rows, int k, int32_t* gmap,
+                         cudaStream_t st) {
+  if (rows <= 0) return kStatusOk;
+  gather_map_kernel<<<grid_for(rows, 256), 256, 0, st>>>(row_asg, rows, k, gmap);
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+}  // namespace moe

@@ -1,0 +1,281 @@
+// Routing: histogram, rounded bin offsets and a stable counting sort of the
+// top-k expert assignments into expert-contiguous order.
+//
+// Restates triton_moe/kernels/fused_cumsum.py:84-171 (torch.sort(stable) +
+// torch.bincount + _cumsum_kernel, with the "down"/"nearest" compaction of
+// :154-169 done on device) and precompute_gather_map
+// (triton_moe/kernels/grouped_gemm.py:104-149) without any host sync.
+//
+// Work is split into "units": contiguous runs of assignments, one warp each.
+//   count   : per-unit per-expert histogram             -> ws[unit][E]
+//   scan    : one CTA; per-expert exclusive scan over units, expert totals,
+//             rounding, bins / padded_bins / offsets, padding-row markers
+//   scatter : per unit, warp-synchronous stable ranks (match_any), writes the
+//             sorted order and both row maps
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "moe_internal.h"
+
+namespace moe {
+namespace {
+
+constexpr int kMaxE = 256;
+constexpr int kWarpsPerBlock = 8;
+
+struct RouteOut {
+  int32_t* bin_ids;
+  int32_t* indices;
+  int32_t* tpe;
+  int32_t* bins;
+  int32_t* padded_bins;
+  int32_t* tok_off;
+  int32_t* ptpe;
+  int32_t* row_asg;
+  long long p_cap;
+  int32_t* asg_row;
+  int* status;
+};
+
+__device__ __forceinline__ int rounded_count(int n, int bs, int mode) {
+  if (mode == 0) return ((n + bs - 1) / bs) * bs;
+  if (mode == 1) return (n / bs) * bs;
+  return ((n + bs / 2) / bs) * bs;
+}
+
+template <typename S>
+__device__ __forceinline__ int load_expert(const S* sel, long long i, int E, int* status) {
+  const long long v = static_cast<long long>(sel[i]);
+  if (v < 0 || v >= E) {
+    if (status) atomicExch(status, kStatusBadExpert);
+    return -1;
+  }
+  return static_cast<int>(v);
+}
+
+// ---- phase 1: per-unit histograms -------------------------------------------
+template <typename S>
+__global__ void route_count_kernel(const S* __restrict__ sel, long long A, int E, long long U,
+                                   long long units, int32_t* __restrict__ ws, int* status) {
+  __shared__ int hist[kWarpsPerBlock][kMaxE];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long unit = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + w;
+  for (int e = lane; e < E; e += 32) hist[w][e] = 0;
+  __syncwarp();
+  if (unit < units) {
+    const long long beg = unit * U, end = min(A, beg + U);
+    for (long long i = beg + lane; i < end; i += 32) {
+      const int e = load_expert(sel, i, E, status);
+      if (e >= 0) atomicAdd(&hist[w][e], 1);
+    }
+    __syncwarp();
+    for (int e = lane; e < E; e += 32) ws[unit * E + e] = hist[w][e];
+  }
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
+__device__ int block_excl_scan(int v, int* total) {
+  __shared__ int warp_sums[32];
+  __shared__ int block_total;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_sums[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    int s = lane < nw ? warp_sums[lane] : 0;
+    int si = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int t = __shfl_up_sync(0xffffffffu, si, o);
+      if (lane >= o) si += t;
+    }
+    if (lane < nw) warp_sums[lane] = si - s;
+    if (lane == nw - 1) block_total = si;
+  }
+  __syncthreads();
+  const int res = warp_sums[w] + incl - v;
+  const int tot = block_total;
+  __syncthreads();
+  if (total) *total = tot;
+  return res;
+}
+
+// ---- phase 2: totals, rounding, offsets, per-unit bases, padding markers ------
+// Launched with one CTA of 1024 threads.  ws[unit][e] becomes the rank of the
+// unit's first assignment to expert e among all assignments to e.
+__global__ void route_scan_kernel(long long units, int E, int bs, int mode, int32_t* ws,
+                                  RouteOut o) {
+  __shared__ int s_n[kMaxE], s_kept[kMaxE], s_pstart[kMaxE], s_padpre[kMaxE + 1];
+  const int tid = threadIdx.x;
+  // per-expert exclusive scan over units: 4 threads per expert column
+  // (E <= 256), each owning a contiguous quarter of the units.
+  constexpr int kParts = 4;
+  const int e = tid % kMaxE, part = tid / kMaxE;
+  const long long per = (units + kParts - 1) / kParts;
+  const long long ub = part * per, ue = min(units, ub + per);
+  int partial = 0;
+  if (e < E)
+    for (long long u = ub; u < ue; ++u) partial += ws[u * E + e];
+  __shared__ int s_part[kParts][kMaxE];
+  s_part[part][e] = partial;
+  __syncthreads();
+  if (e < E) {
+    int run = 0;
+    for (int p = 0; p < part; ++p) run += s_part[p][e];
+    for (long long u = ub; u < ue; ++u) {
+      const int c = ws[u * E + e];
+      ws[u * E + e] = run;
+      run += c;
+    }
+    if (part == kParts - 1) {
+      s_n[e] = run;
+    }
+  }
+  __syncthreads();
+  // expert-level values and the two cumulative sums (threads 0..255 hold experts)
+  int n = 0, r = 0, kept = 0, pads = 0;
+  if (tid < E) {
+    n = s_n[tid];
+    r = rounded_count(n, bs, mode);
+    kept = min(n, r);
+    pads = r - kept;
+  }
+  int tot_kept, tot_round, tot_pad;
+  const int kept_ex = block_excl_scan(tid < kMaxE ? kept : 0, &tot_kept);
+  const int round_ex = block_excl_scan(tid < kMaxE ? r : 0, &tot_round);
+  const int pad_ex = block_excl_scan(tid < kMaxE ? pads : 0, &tot_pad);
+  if (tid < E) {
+    s_kept[tid] = kept;
+    s_pstart[tid] = round_ex;
+    s_padpre[tid] = pad_ex;
+    o.tpe[tid] = n;
+    o.bins[tid] = kept_ex + kept;
+    o.padded_bins[tid] = round_ex + r;
+    o.tok_off[tid] = round_ex;
+    o.ptpe[tid] = r;
+    if (tid == E - 1) o.tok_off[E] = round_ex + r;
+  }
+  if (tid == 0) s_padpre[E] = tot_pad;
+  __syncthreads();
+  if (o.row_asg != nullptr) {
+    if (static_cast<long long>(tot_round) > o.p_cap) {
+      if (tid == 0 && o.status) atomicExch(o.status, kStatusCapacity);
+    } else {
+      // mark padding rows with -1: flatten all pads and binary-search the expert
+      for (int p = tid; p < tot_pad; p += blockDim.x) {
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+          int mid = (lo + hi + 1) >> 1;
+          if (s_padpre[mid] <= p) lo = mid;
+          else hi = mid - 1;
+        }
+        const int row = s_pstart[lo] + s_kept[lo] + (p - s_padpre[lo]);
+        o.row_asg[row] = -1;
+      }
+    }
+  }
+}
+
+// ---- phase 3: stable scatter ---------------------------------------------------
+template <typename S>
+__global__ void route_scatter_kernel(const S* __restrict__ sel, long long A, int E, long long U,
+                                     long long units, const int32_t* __restrict__ ws,
+                                     RouteOut o) {
+  __shared__ int base[kWarpsPerBlock][kMaxE];
+  __shared__ int s_bstart[kMaxE], s_pstart[kMaxE], s_kept[kMaxE];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int b_end = o.bins[e];
+    const int b_prev = e > 0 ? o.bins[e - 1] : 0;
+    s_bstart[e] = b_prev;
+    s_kept[e] = b_end - b_prev;
+    s_pstart[e] = o.tok_off[e];
+  }
+  const long long unit = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + w;
+  if (unit < units)
+    for (int e = lane; e < E; e += 32) base[w][e] = ws[unit * E + e];
+  __syncthreads();
+  if (unit >= units) return;
+  const bool write_rows =
+      o.row_asg != nullptr && static_cast<long long>(o.tok_off[E]) <= o.p_cap;
+  const long long beg = unit * U, end = min(A, beg + U);
+  for (long long i0 = beg; i0 < end; i0 += 32) {
+    const long long i = i0 + lane;
+    const bool valid = i < end;
+    const int e = valid ? load_expert(sel, i, E, nullptr) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0) {
+      const int rank = base[w][e] + rank_in;
+      if (rank < s_kept[e]) {
+        const int pos = s_bstart[e] + rank;
+        o.bin_ids[pos] = e;
+        o.indices[pos] = static_cast<int32_t>(i);
+        const int row = s_pstart[e] + rank;
+        if (write_rows) o.row_asg[row] = static_cast<int32_t>(i);
+        if (o.asg_row) o.asg_row[i] = row;
+      } else if (o.asg_row) {
+        o.asg_row[i] = -1;  // dropped by "down"/"nearest" rounding
+      }
+    } else if (valid && o.asg_row) {
+      o.asg_row[i] = -1;
+    }
+    __syncwarp();
+    const int leader = 31 - __clz(peers);
+    if (e >= 0 && lane == leader) base[w][e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+long long unit_size(long long A) {
+  // at most 256 units; at least 256 assignments (8 warp-steps) per unit
+  long long U = (A + 255) / 256;
+  if (U < 256) U = 256;
+  return (U + 31) / 32 * 32;
+}
+
+}  // namespace
+
+long long route_workspace_bytes(long long A, int E) {
+  const long long U = unit_size(A);
+  const long long units = (A + U - 1) / U;
+  return (units > 0 ? units : 1) * E * 4;
+}
+
+template <typename S>
+static int route_impl(const S* sel, long long A, int E, int bs, int mode, const RouteOut& o,
+                      void* ws, long long ws_bytes, cudaStream_t st) {
+  const long long U = unit_size(A);
+  const long long units = (A + U - 1) / U;
+  if (ws_bytes < route_workspace_bytes(A, E)) return kStatusBadArg;
+  int32_t* w = static_cast<int32_t*>(ws);
+  const int blocks = static_cast<int>((units + kWarpsPerBlock - 1) / kWarpsPerBlock);
+  if (units > 0)
+    route_count_kernel<S><<<blocks, kWarpsPerBlock * 32, 0, st>>>(sel, A, E, U, units, w, o.status);
+  route_scan_kernel<<<1, 1024, 0, st>>>(units, E, bs, mode, w, o);
+  if (units > 0)
+    route_scatter_kernel<S><<<blocks, kWarpsPerBlock * 32, 0, st>>>(sel, A, E, U, units, w, o);
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+int route(const void* sel, int sel_is_int64, long long A, int E, int bs, int mode,
+          int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins, int32_t* padded_bins,
+          int32_t* tok_off, int32_t* ptpe, int32_t* row_asg, long long p_cap, int32_t* asg_row,
+          void* ws, long long ws_bytes, int* status, cudaStream_t st) {
+  if (E <= 0 || E > kMaxE || A < 0 || bs <= 0 || mode < 0 || mode > 2) return kStatusBadArg;
+  if (!tpe || !bins || !padded_bins || !tok_off || !ptpe) return kStatusBadArg;
+  if (A > 0 && (!sel || !bin_ids || !indices)) return kStatusBadArg;
+  RouteOut o{bin_ids, indices, tpe, bins, padded_bins, tok_off, ptpe, row_asg, p_cap, asg_row, status};
+  if (sel_is_int64)
+    return route_impl(static_cast<const long long*>(sel), A, E, bs, mode, o, ws, ws_bytes, st);
+  return route_impl(static_cast<const int32_t*>(sel), A, E, bs, mode, o, ws, ws_bytes, st);
+}
+
+}  // namespace moe

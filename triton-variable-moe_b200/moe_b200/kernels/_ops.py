@@ -1,0 +1,305 @@
+"""Tensor-level wrappers of the libmoe_b200 C ABI.
+
+These functions take torch tensors, validate them, and launch on the current
+CUDA stream.  They never synchronise the host.  Outputs may be passed in
+(`out=`) so that callers can reuse or pre-size buffers (the module path sizes
+every token-space buffer by an upper bound so that nothing depends on
+device-side counts).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .._lib import (
+    ACT_CODE,
+    DTYPE_CODE,
+    ROUND_CODE,
+    check,
+    lib,
+    ptr,
+    require_cuda,
+    stream_handle,
+)
+
+_GEMM_DTYPES = (torch.bfloat16, torch.float16)
+
+_status_bufs: dict[int, torch.Tensor] = {}
+
+
+def status_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word that kernels set when they detect a device-side
+    error (bad expert id, row-capacity overflow, a bounded wait giving up)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status_bufs.get(idx)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_bufs[idx] = buf
+    return buf
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Synchronising check of the device status word; raises and clears it."""
+    from .._lib import MoEKernelError, STATUS_TEXT
+
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    buf = status_buffer(device)
+    v = int(buf.item())
+    if v != 0:
+        buf.zero_()
+        raise MoEKernelError(f"device-side error: {STATUS_TEXT.get(v, v)} (status {v})")
+
+
+def padded_capacity(num_assignments: int, num_experts: int, block_size: int) -> int:
+    """Upper bound of the padded row count for any routing outcome."""
+    return num_assignments + num_experts * (block_size - 1)
+
+
+@dataclass
+class Routing:
+    bin_ids: torch.Tensor  # [A] int32 (first bins[-1] valid)
+    indices: torch.Tensor  # [A] int32
+    tokens_per_expert: torch.Tensor  # [E] int32
+    bins: torch.Tensor  # [E] int32
+    padded_bins: torch.Tensor  # [E] int32
+    expert_token_offsets: torch.Tensor  # [E+1] int32
+    padded_tokens_per_expert: torch.Tensor  # [E] int32
+    row_to_assignment: torch.Tensor | None  # [p_capacity] int32
+    assignment_to_row: torch.Tensor | None  # [A] int32
+    p_capacity: int
+
+
+def route(
+    selected_experts: torch.Tensor,
+    num_experts: int,
+    block_size: int,
+    rounding: str = "up",
+    want_rows: bool = True,
+) -> Routing:
+    require_cuda(selected_experts)
+    sel = selected_experts.reshape(-1)
+    if sel.dtype not in (torch.int32, torch.int64):
+        sel = sel.to(torch.int32)
+    sel = sel.contiguous()
+    A = sel.numel()
+    E = int(num_experts)
+    dev = sel.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    bin_ids = torch.empty(A, **i32)
+    indices = torch.empty(A, **i32)
+    meta = torch.empty(5 * E + 1, **i32)  # one allocation for the small outputs
+    tpe, bins, pbins, ptpe = meta[:E], meta[E : 2 * E], meta[2 * E : 3 * E], meta[3 * E : 4 * E]
+    tok_off = meta[4 * E :]
+    cap = padded_capacity(A, E, block_size)
+    row_asg = torch.empty(max(cap, 1), **i32) if want_rows else None
+    asg_row = torch.empty(max(A, 1), **i32) if want_rows else None
+    ws_bytes = int(lib.moe_route_workspace_bytes(A, E))
+    ws = torch.empty((ws_bytes + 3) // 4, **i32)
+    rc = lib.moe_route(
+        ptr(sel), 1 if sel.dtype == torch.int64 else 0, A, E, int(block_size), ROUND_CODE[rounding],
+        ptr(bin_ids), ptr(indices), ptr(tpe), ptr(bins), ptr(pbins), ptr(tok_off), ptr(ptpe),
+        ptr(row_asg), cap, ptr(asg_row), ptr(ws), ws_bytes, ptr(status_buffer(dev)),
+        stream_handle(dev),
+    )
+    check(rc, "moe_route")
+    return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
+
+
+def build_row_map(
+    indices: torch.Tensor,
+    bin_ids: torch.Tensor,
+    bins: torch.Tensor,
+    padded_bins: torch.Tensor,
+    padded_rows: int,
+    num_assignments: int,
+    want_row_to_assignment: bool = True,
+    want_assignment_to_row: bool = True,
+) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    require_cuda(indices, bin_ids, bins, padded_bins)
+    dev = indices.device
+    ind = indices.to(torch.int32).contiguous()
+    bid = bin_ids.to(torch.int32).contiguous()
+    b = bins.to(torch.int32).contiguous()
+    pb = padded_bins.to(torch.int32).contiguous()
+    r2a = torch.empty(max(padded_rows, 1), dtype=torch.int32, device=dev) if want_row_to_assignment else None
+    a2r = torch.empty(max(num_assignments, 1), dtype=torch.int32, device=dev) if want_assignment_to_row else None
+    rc = lib.moe_build_row_map(
+        ptr(ind), ptr(bid), ptr(b), ptr(pb), ind.numel(), padded_rows, ptr(r2a),
+        num_assignments, ptr(a2r), ptr(status_buffer(dev)), stream_handle(dev),
+    )
+    check(rc, "moe_build_row_map")
+    return r2a, a2r
+
+
+def gather_map(row_to_assignment: torch.Tensor, padded_rows: int, top_k: int) -> torch.Tensor:
+    dev = row_to_assignment.device
+    out = torch.empty(padded_rows, dtype=torch.int32, device=dev)
+    check(lib.moe_gather_map(ptr(row_to_assignment), padded_rows, top_k, ptr(out), stream_handle(dev)),
+          "moe_gather_map")
+    return out
+
+
+def gather(
+    x: torch.Tensor,
+    row_map: torch.Tensor,
+    map_div: int,
+    rows: int,
+    out: torch.Tensor | None = None,
+    rows_device: torch.Tensor | None = None,
+    weights: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """out[r] = x[row_map[r] // map_div] (* weights[row_map[r]]), zero where row_map < 0."""
+    require_cuda(x, row_map)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    H = x.shape[1]
+    if out is None:
+        out = torch.empty(rows, H, dtype=x.dtype, device=x.device)
+    if weights is not None:
+        weights = weights.to(x.dtype).contiguous()
+    rc = lib.moe_padded_gather(
+        ptr(x), x.stride(0), H, ptr(row_map), int(map_div), int(rows), ptr(rows_device),
+        ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[x.dtype], stream_handle(x.device),
+    )
+    check(rc, "moe_padded_gather")
+    return out
+
+
+def combine(
+    y: torch.Tensor,
+    assignment_to_row: torch.Tensor,
+    num_tokens: int,
+    top_k: int,
+    weights: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """out[t] = sum_j round(y[row(t, j)] * w[t*k+j]) (unit weights when None)."""
+    require_cuda(y, assignment_to_row)
+    if y.stride(-1) != 1:
+        y = y.contiguous()
+    H = y.shape[1]
+    if out is None:
+        out = torch.empty(num_tokens, H, dtype=y.dtype, device=y.device)
+    if weights is not None:
+        weights = weights.to(y.dtype).contiguous()
+    rc = lib.moe_padded_scatter(
+        ptr(y), y.stride(0), H, ptr(assignment_to_row), int(num_tokens), int(top_k),
+        ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[y.dtype], stream_handle(y.device),
+    )
+    check(rc, "moe_padded_scatter")
+    return out
+
+
+def relu_squared_grad(grad_out: torch.Tensor, pre_act: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    require_cuda(grad_out, pre_act)
+    g = grad_out.contiguous()
+    p = pre_act.to(g.dtype).contiguous()
+    if out is None:
+        out = torch.empty_like(g)
+    rc = lib.moe_relu_squared_grad(ptr(g), ptr(p), g.shape[0], g.shape[1], g.stride(0), ptr(out),
+                                   DTYPE_CODE[g.dtype], stream_handle(g.device))
+    check(rc, "moe_relu_squared_grad")
+    return out
+
+
+def _gemm_check(*ts: torch.Tensor) -> None:
+    require_cuda(*ts)
+    dt = ts[0].dtype
+    for t in ts:
+        if t.dtype != dt:
+            raise TypeError(f"grouped GEMM operands must share a dtype, got {dt} and {t.dtype}")
+        if t.stride(-1) != 1:
+            raise ValueError("grouped GEMM operands must be row-major contiguous in the last dim")
+    if dt not in _GEMM_DTYPES:
+        raise NotImplementedError(
+            f"grouped GEMM dtype {dt}: the sm_100a kernels compute in bf16/fp16 with fp32 accumulation"
+        )
+
+
+def _meta(t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    return t if (t.dtype == torch.int32 and t.is_contiguous()) else t.to(torch.int32).contiguous()
+
+
+def gemm_up(x, w1, tok_off, w_off, tok_cnt, num_experts, activation, out, pre_act=None, tile_n=0):
+    _gemm_check(x, w1, out)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    H, TW = w1.shape
+    rc = lib.moe_grouped_gemm_up(
+        ptr(x), x.shape[0], x.stride(0), ptr(w1), H, TW, ptr(tok_off), ptr(w_off), ptr(tok_cnt),
+        int(num_experts), ACT_CODE[activation], ptr(out), ptr(pre_act), out.stride(0),
+        DTYPE_CODE[x.dtype], int(tile_n), ptr(status_buffer(x.device)), stream_handle(x.device),
+    )
+    check(rc, "moe_grouped_gemm_up")
+    return out
+
+
+def gemm_down(inter, w2, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0):
+    _gemm_check(inter, w2, out)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    TW, H = w2.shape
+    rc = lib.moe_grouped_gemm_down(
+        ptr(inter), inter.shape[0], inter.stride(0), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
+        ptr(tok_cnt), int(num_experts), ptr(out), out.stride(0), DTYPE_CODE[inter.dtype],
+        int(tile_n), ptr(status_buffer(inter.device)), stream_handle(inter.device),
+    )
+    check(rc, "moe_grouped_gemm_down")
+    return out
+
+
+def gemm_up_dx(grad_act, w1, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0):
+    _gemm_check(grad_act, w1, out)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    H, TW = w1.shape
+    rc = lib.moe_grouped_gemm_up_dx(
+        ptr(grad_act), grad_act.shape[0], grad_act.stride(0), ptr(w1), H, TW, ptr(tok_off),
+        ptr(w_off), ptr(tok_cnt), int(num_experts), ptr(out), out.stride(0),
+        DTYPE_CODE[grad_act.dtype], int(tile_n), ptr(status_buffer(w1.device)),
+        stream_handle(w1.device),
+    )
+    check(rc, "moe_grouped_gemm_up_dx")
+    return out
+
+
+def gemm_up_dw(x, grad_act, tok_off, w_off, num_experts, out, tile_n=0):
+    _gemm_check(x, grad_act, out)
+    tok_off, w_off = _meta(tok_off), _meta(w_off)
+    H, TW = out.shape
+    rc = lib.moe_grouped_gemm_up_dw(
+        ptr(x), x.shape[0], x.stride(0), ptr(grad_act), grad_act.stride(0), H, TW, ptr(tok_off),
+        ptr(w_off), int(num_experts), ptr(out), DTYPE_CODE[x.dtype], int(tile_n),
+        ptr(status_buffer(x.device)), stream_handle(x.device),
+    )
+    check(rc, "moe_grouped_gemm_up_dw")
+    return out
+
+
+def gemm_down_dinter(grad_y, w2, tok_off, w_off, tok_cnt, num_experts, out, pre_act=None, tile_n=0):
+    _gemm_check(grad_y, w2, out)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    TW, H = w2.shape
+    ld_pre = pre_act.stride(0) if pre_act is not None else 0
+    rc = lib.moe_grouped_gemm_down_dinter(
+        ptr(grad_y), grad_y.shape[0], grad_y.stride(0), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
+        ptr(tok_cnt), int(num_experts), ptr(pre_act), ld_pre, ptr(out), out.stride(0),
+        DTYPE_CODE[grad_y.dtype], int(tile_n), ptr(status_buffer(w2.device)),
+        stream_handle(w2.device),
+    )
+    check(rc, "moe_grouped_gemm_down_dinter")
+    return out
+
+
+def gemm_down_dw(inter, grad_y, tok_off, w_off, num_experts, out, tile_n=0):
+    _gemm_check(inter, grad_y, out)
+    tok_off, w_off = _meta(tok_off), _meta(w_off)
+    TW, H = out.shape
+    rc = lib.moe_grouped_gemm_down_dw(
+        ptr(inter), inter.shape[0], inter.stride(0), ptr(grad_y), grad_y.stride(0), H, TW,
+        ptr(tok_off), ptr(w_off), int(num_experts), ptr(out), DTYPE_CODE[inter.dtype], int(tile_n),
+        ptr(status_buffer(inter.device)), stream_handle(inter.device),
+    )
+    check(rc, "moe_grouped_gemm_down_dw")
+    return out
