@@ -1,0 +1,490 @@
+"""Benchmark: MoE layer forward + backward tokens/s on B200 (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config c3]
+
+A step is one training pass of the MoE layer over one synthetic batch:
+`out, aux, f_i = layer(x); out.backward(g)` (router, routing, gather, grouped
+GEMM up with relu^2, grouped GEMM down, weighted combine, and the full
+backward).  The default workload is BASELINE config 3, the north-star
+768-hidden variable-expert layer: n_embd=768, experts 4x512 + 8x256 + 4x128,
+top-2, batch 8 x seq 1024 = 8192 tokens, bf16, x ~ N(0,1), weights N(0,0.02),
+router from a random-init linear.
+
+Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
+events on the launch stream, with a 256 MiB write between steps to flush the
+126 MB L2; barrier + synchronize on both sides; the per-rank time is the sum
+of the K step times and the job time is the max over ranks.  `value` =
+tokens processed by all ranks / job time.  At N > 1 each rank runs its own
+replica of the workload (no collective on the data path): scaling "weak".
+
+Extra keys: `roofline` (the grouped-GEMM engine: algorithmic FLOPs
+12*H*sum_e n_e*w_e per step / summed device time of its 6 launches per step,
+against the measured bf16 peak), `cpu_baseline` (the numpy CPU oracle on the
+host cores), `e2e` (pinned host input -> device, fwd+bwd, output -> host,
+per step), `gpu_launches`, `clocks`.
+
+`--impl reference` times the reference algorithm's CPU restatement (the
+oracle; the reference itself is Triton/Python and cannot run on the host
+outside the Triton interpreter) on the host cores for the same config and
+metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "triton-variable-moe_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE layer fwd+bwd tokens/s"
+
+CONFIGS = {
+    "c2u": dict(n_embd=256, expert_sizes=[(8, 512)], top_k=2, batch=8, seq=512, zipf=False),
+    "c2v": dict(n_embd=256, expert_sizes=[(4, 512), (4, 256)], top_k=2, batch=8, seq=512, zipf=False),
+    "c3": dict(n_embd=768, expert_sizes=[(4, 512), (8, 256), (4, 128)], top_k=2, batch=8, seq=1024,
+               zipf=False),
+    "c4": dict(n_embd=2048, expert_sizes=[(64, 1024)], top_k=8, batch=1, seq=16384, zipf=True),
+    "c5": dict(n_embd=4096, expert_sizes=[(32, 2048), (64, 1024), (32, 512)], top_k=8, batch=1,
+               seq=65536, zipf=True),
+}
+
+
+def workload_name(name: str, cfg: dict) -> str:
+    sizes = "+".join(f"{c}x{w}" for c, w in cfg["expert_sizes"])
+    return (f"{name}: MoE layer n_embd={cfg['n_embd']} experts {sizes} top-{cfg['top_k']} "
+            f"tokens={cfg['batch'] * cfg['seq']}" + (" zipf(1.1) router bias" if cfg["zipf"] else ""))
+
+
+def widths_of(cfg):
+    return [w for c, w in cfg["expert_sizes"] for _ in range(c)]
+
+
+def gemm_flops(tokens_per_expert, cfg) -> float:
+    """12 * H * sum_e n_e * w_e: the six GEMMs of fwd+bwd, unpadded counts."""
+    H = cfg["n_embd"]
+    return float(sum(12 * H * int(n) * w for n, w in zip(tokens_per_expert, widths_of(cfg))))
+
+
+def permute_bytes(cfg) -> float:
+    """Unique bytes moved by gather + scatter forward and their backward mirrors."""
+    T = cfg["batch"] * cfg["seq"]
+    A = T * cfg["top_k"]
+    H = cfg["n_embd"]
+    return float(4 * (T + A) * H * 2 + 2 * A * 2)
+
+
+def zipf_bias(E, seed, s=1.1):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    ranks = torch.randperm(E, generator=g).float() + 1.0
+    logp = -s * torch.log(ranks)
+    logp = logp - torch.logsumexp(logp, 0)
+    return logp - logp.mean()
+
+
+def build_layer(cfg, device, seed=0):
+    import torch
+
+    from moe_b200 import TritonMoEConfig, TritonMoEMLP
+
+    torch.manual_seed(seed)
+    layer = TritonMoEMLP(TritonMoEConfig(n_embd=cfg["n_embd"], expert_sizes=cfg["expert_sizes"],
+                                         num_active_experts=cfg["top_k"], block_size=64))
+    with torch.no_grad():
+        layer.router.weight.normal_(0, 0.02)
+        layer.w1.normal_(0, 0.02)
+        layer.w2.normal_(0, 0.02)
+    if cfg["zipf"]:
+        r = torch.nn.Linear(cfg["n_embd"], layer.num_experts, bias=True)
+        with torch.no_grad():
+            r.weight.copy_(layer.router.weight)
+            r.bias.copy_(zipf_bias(layer.num_experts, seed + 1))
+        layer.router = r
+    return layer.to(device=device, dtype=torch.bfloat16)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, power, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            p = [v.strip() for v in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = float(p[2])
+                power.append(float(p[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [s for s, pw in zip(sm, power) if pw > 200.0] or sm
+        return {
+            "sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": smax,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+            "power_w_max": max(power) if power else None,
+        }
+
+
+# ------------------------------------------------------------------ helpers
+def gpu_selector(dev) -> str:
+    """nvidia-smi -i selector (PCI bus id) of a torch device, robust to
+    CUDA_VISIBLE_DEVICES renumbering."""
+    import torch
+
+    p = torch.cuda.get_device_properties(dev)
+    try:
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except AttributeError:
+        return str(dev.index)
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def ncu_traffic(workload: str):
+    """DRAM bytes per step of the grouped-GEMM launches from the committed ncu
+    summary (profiles/grouped_gemm_<workload>.md, line `dram_bytes_per_step: N`)."""
+    p = ROOT / "profiles" / f"grouped_gemm_{workload}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_step:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except (ValueError, IndexError):
+                return None
+    return None
+
+
+def cpu_oracle_step(cfg, x_np, w1, w2, sel, wts, g_np):
+    from oracle import moe_oracle as orc
+
+    orc.moe_mlp(x_np, w1, w2, sel, wts, widths_of(cfg), cfg["top_k"], 64, grad_out=g_np, dtype="bf16")
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_sample(cfg, tokens: int, seed=0):
+    """Inputs for the CPU oracle on a `tokens`-token slice of the workload."""
+    import numpy as np
+    import torch
+
+    layer = build_layer(cfg, "cpu", seed).float()
+    g = torch.Generator().manual_seed(seed + 7)
+    x = torch.randn(tokens, cfg["n_embd"], generator=g)
+    with torch.no_grad():
+        logits = layer.router(x.bfloat16().float())
+        probs = torch.sigmoid(logits)
+        w, sel = torch.topk(probs, cfg["top_k"], dim=-1)
+        w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    gout = torch.randn(tokens, cfg["n_embd"], generator=g)
+    return (x.numpy(), layer.w1.detach().numpy(), layer.w2.detach().numpy(),
+            sel.reshape(-1).numpy().astype(np.int64), w.reshape(-1).numpy(), gout.numpy())
+
+
+def time_cpu_oracle(cfg, budget_s=15.0, tokens=None):
+    T = cfg["batch"] * cfg["seq"]
+    tokens = tokens or min(T, 4096)
+    args = cpu_sample(cfg, tokens)
+    t0 = time.perf_counter()
+    cpu_oracle_step(cfg, *args)  # warm-up (first-call allocation)
+    first = time.perf_counter() - t0
+    reps = max(1, min(20, int(budget_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        cpu_oracle_step(cfg, *args)
+    dt = (time.perf_counter() - t0) / reps
+    return tokens / dt, tokens, reps
+
+
+# ------------------------------------------------------------------ arms
+def run_reference(args, cfg, name):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    T = cfg["batch"] * cfg["seq"]
+    tokens = min(T, 2048)
+    xs = cpu_sample(cfg, tokens)
+    for _ in range(args.warmup):
+        cpu_oracle_step(cfg, *xs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_oracle_step(cfg, *xs)
+    dt = time.perf_counter() - t0
+    value = tokens * args.steps / dt
+    cores = cpu_threads()
+    sample = (f"{tokens} of the workload's {T} tokens per step (bf16-rounded fp32 numpy "
+              f"restatement of the reference algorithm, fwd+bwd)")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": workload_name(name, cfg), "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, cfg, name):
+    import torch
+    import torch.distributed as dist
+
+    from moe_b200.kernels import _ops
+
+    ws, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    T = cfg["batch"] * cfg["seq"]
+    H = cfg["n_embd"]
+    layer = build_layer(cfg, dev, seed=0)
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    x_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
+    g_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev).requires_grad_(True)
+    gout = g_host.to(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step(xi, gi):
+        layer.zero_grad(set_to_none=True)
+        xi.grad = None
+        out, aux, f_i = layer(xi)
+        out.backward(gi)
+        return out
+
+    for _ in range(max(args.warmup, 3)):
+        step(x, gout)
+    torch.cuda.synchronize()
+
+    # clock samples: a ~1.5 s soak of the same step right before the timed loop
+    sampler = ClockSampler(gpu_selector(dev))
+    sampler.start()
+    t_end = time.perf_counter() + 1.5
+    while time.perf_counter() < t_end:
+        step(x, gout)
+        torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = _ops.launch_count
+    for i in range(args.steps):
+        flush.zero_()  # 256 MiB write: evicts the 126 MB L2 between timed steps
+        starts[i].record()
+        step(x, gout)
+        ends[i].record()
+    torch.cuda.synchronize()
+    launches = _ops.launch_count - l0
+    if ws > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    job_ms = float(t.item())
+    ms_per_step = job_ms / args.steps
+    value = T * ws * args.steps / (job_ms / 1e3)
+
+    # grouped-GEMM roofline: per-launch CUDA events over instrumented steps
+    with torch.no_grad():
+        _, _, _, sel = layer._route_weights(x.detach().reshape(-1, H))
+        tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts).cpu().tolist()
+    flops = gemm_flops(tpe, cfg)
+    reps = 5
+    gemm_ms = 0.0
+    for _ in range(reps):
+        flush.zero_()
+        with _ops.record_gemm_events() as evs:
+            step(x, gout)
+        torch.cuda.synchronize()
+        gemm_ms += sum(s.elapsed_time(e) for _, s, e in evs)
+    gemm_ms /= reps
+    n_gemm_launches = 6
+    peak_tf, peak_hbm, peak_kind = measured_peaks()
+    achieved = flops / (gemm_ms / 1e3) / 1e12
+    traffic_step = ncu_traffic(name)
+    roofline = {
+        "kernel": "grouped_gemm_kernel (tcgen05; 6 launches per step: up, down, down-dX, "
+                  "down-dW, up-dX, up-dW)",
+        "bound": "tensor",
+        "achieved": achieved,
+        "peak": peak_tf,
+        "unit": "TFLOP/s",
+        "frac": achieved / peak_tf,
+        "peak_source": f"{peak_kind} bf16 dense (burst)",
+        "flops_per_launch": flops / n_gemm_launches,
+        "avg_launch_ms": gemm_ms / n_gemm_launches,
+        "traffic": (traffic_step / n_gemm_launches) if traffic_step else None,
+    }
+
+    # end to end through the public API with host buffers
+    out_host = torch.empty(cfg["batch"], cfg["seq"], H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x.detach())
+    gd = torch.empty_like(gout)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        e_starts[i].record()
+        xd.copy_(x_host, non_blocking=True)
+        gd.copy_(g_host, non_blocking=True)
+        xi = xd.detach().requires_grad_(True)
+        out = step(xi, gd)
+        out_host.copy_(out.detach(), non_blocking=True)
+        e_ends[i].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = T * ws * args.steps / (float(t.item()) / 1e3)
+    nbytes = x_host.numel() * 2
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        v, tokens, creps = time_cpu_oracle(cfg)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"{tokens} of {T} tokens, fwd+bwd, {creps} reps (numpy oracle, bf16 "
+                         "rounding points)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) random-init weights)",
+            "config": {
+                "workload": workload_name(name, cfg),
+                "global_batch": cfg["batch"] * ws,
+                "seq_len": cfg["seq"],
+                "parallelism": f"{ws} independent replica(s)" if ws > 1 else "single GPU",
+                "l2": "flushed by a 256 MiB write between timed steps",
+            },
+            "roofline": roofline,
+            "gemm_frac_of_bf16_peak": roofline["frac"],
+            "permute_bytes_per_step": permute_bytes(cfg),
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
+                    "d2h_bytes_per_step": nbytes},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg, args.config)
+    return run_b200(args, cfg, args.config)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

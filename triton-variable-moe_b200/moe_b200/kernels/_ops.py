@@ -9,6 +9,7 @@ device-side counts).
 
 from __future__ import annotations
 
+from contextlib import contextmanager
 from dataclasses import dataclass
 
 import torch
@@ -27,6 +28,45 @@ from .._lib import (
 _GEMM_DTYPES = (torch.bfloat16, torch.float16)
 
 _status_bufs: dict[int, torch.Tensor] = {}
+
+# Number of CUDA kernels launched through this module (host-side count; the
+# routing entry point launches three).  bench.py reports it per timed region.
+launch_count = 0
+
+
+def _count(n: int = 1) -> None:
+    global launch_count
+    launch_count += n
+
+
+_gemm_events: list | None = None
+
+
+@contextmanager
+def record_gemm_events():
+    """Within the block, every grouped GEMM launch is bracketed by CUDA events
+    on its launch stream; yields the list of (name, start, end) events."""
+    global _gemm_events
+    prev, _gemm_events = _gemm_events, []
+    try:
+        yield _gemm_events
+    finally:
+        _gemm_events = prev
+
+
+def _ev_begin():
+    if _gemm_events is None:
+        return None
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    return e
+
+
+def _ev_end(start, name: str) -> None:
+    if start is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        _gemm_events.append((name, start, e))
 
 
 def status_buffer(device: torch.device) -> torch.Tensor:
@@ -104,6 +144,7 @@ def route(
         stream_handle(dev),
     )
     check(rc, "moe_route")
+    _count(3)
     return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
 
 
@@ -130,6 +171,7 @@ def build_row_map(
         num_assignments, ptr(a2r), ptr(status_buffer(dev)), stream_handle(dev),
     )
     check(rc, "moe_build_row_map")
+    _count(1)
     return r2a, a2r
 
 
@@ -138,6 +180,7 @@ def gather_map(row_to_assignment: torch.Tensor, padded_rows: int, top_k: int) ->
     out = torch.empty(padded_rows, dtype=torch.int32, device=dev)
     check(lib.moe_gather_map(ptr(row_to_assignment), padded_rows, top_k, ptr(out), stream_handle(dev)),
           "moe_gather_map")
+    _count()
     return out
 
 
@@ -164,6 +207,7 @@ def gather(
         ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[x.dtype], stream_handle(x.device),
     )
     check(rc, "moe_padded_gather")
+    _count(1)
     return out
 
 
@@ -189,6 +233,7 @@ def combine(
         ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[y.dtype], stream_handle(y.device),
     )
     check(rc, "moe_padded_scatter")
+    _count(1)
     return out
 
 
@@ -201,6 +246,7 @@ def relu_squared_grad(grad_out: torch.Tensor, pre_act: torch.Tensor, out: torch.
     rc = lib.moe_relu_squared_grad(ptr(g), ptr(p), g.shape[0], g.shape[1], g.stride(0), ptr(out),
                                    DTYPE_CODE[g.dtype], stream_handle(g.device))
     check(rc, "moe_relu_squared_grad")
+    _count(1)
     return out
 
 
@@ -228,12 +274,15 @@ def gemm_up(x, w1, tok_off, w_off, tok_cnt, num_experts, activation, out, pre_ac
     _gemm_check(x, w1, out)
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
     H, TW = w1.shape
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_up(
         ptr(x), x.shape[0], x.stride(0), ptr(w1), H, TW, ptr(tok_off), ptr(w_off), ptr(tok_cnt),
         int(num_experts), ACT_CODE[activation], ptr(out), ptr(pre_act), out.stride(0),
         DTYPE_CODE[x.dtype], int(tile_n), ptr(status_buffer(x.device)), stream_handle(x.device),
     )
+    _ev_end(ev, "grouped_gemm_up")
     check(rc, "moe_grouped_gemm_up")
+    _count(1)
     return out
 
 
@@ -241,12 +290,15 @@ def gemm_down(inter, w2, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0):
     _gemm_check(inter, w2, out)
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
     TW, H = w2.shape
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_down(
         ptr(inter), inter.shape[0], inter.stride(0), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
         ptr(tok_cnt), int(num_experts), ptr(out), out.stride(0), DTYPE_CODE[inter.dtype],
         int(tile_n), ptr(status_buffer(inter.device)), stream_handle(inter.device),
     )
+    _ev_end(ev, "grouped_gemm_down")
     check(rc, "moe_grouped_gemm_down")
+    _count(1)
     return out
 
 
@@ -254,13 +306,16 @@ def gemm_up_dx(grad_act, w1, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0
     _gemm_check(grad_act, w1, out)
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
     H, TW = w1.shape
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_up_dx(
         ptr(grad_act), grad_act.shape[0], grad_act.stride(0), ptr(w1), H, TW, ptr(tok_off),
         ptr(w_off), ptr(tok_cnt), int(num_experts), ptr(out), out.stride(0),
         DTYPE_CODE[grad_act.dtype], int(tile_n), ptr(status_buffer(w1.device)),
         stream_handle(w1.device),
     )
+    _ev_end(ev, "grouped_gemm_up_dx")
     check(rc, "moe_grouped_gemm_up_dx")
+    _count(1)
     return out
 
 
@@ -268,12 +323,15 @@ def gemm_up_dw(x, grad_act, tok_off, w_off, num_experts, out, tile_n=0):
     _gemm_check(x, grad_act, out)
     tok_off, w_off = _meta(tok_off), _meta(w_off)
     H, TW = out.shape
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_up_dw(
         ptr(x), x.shape[0], x.stride(0), ptr(grad_act), grad_act.stride(0), H, TW, ptr(tok_off),
         ptr(w_off), int(num_experts), ptr(out), DTYPE_CODE[x.dtype], int(tile_n),
         ptr(status_buffer(x.device)), stream_handle(x.device),
     )
+    _ev_end(ev, "grouped_gemm_up_dw")
     check(rc, "moe_grouped_gemm_up_dw")
+    _count(1)
     return out
 
 
@@ -282,13 +340,16 @@ def gemm_down_dinter(grad_y, w2, tok_off, w_off, tok_cnt, num_experts, out, pre_
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
     TW, H = w2.shape
     ld_pre = pre_act.stride(0) if pre_act is not None else 0
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_down_dinter(
         ptr(grad_y), grad_y.shape[0], grad_y.stride(0), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
         ptr(tok_cnt), int(num_experts), ptr(pre_act), ld_pre, ptr(out), out.stride(0),
         DTYPE_CODE[grad_y.dtype], int(tile_n), ptr(status_buffer(w2.device)),
         stream_handle(w2.device),
     )
+    _ev_end(ev, "grouped_gemm_down_dinter")
     check(rc, "moe_grouped_gemm_down_dinter")
+    _count(1)
     return out
 
 
@@ -296,10 +357,13 @@ def gemm_down_dw(inter, grad_y, tok_off, w_off, num_experts, out, tile_n=0):
     _gemm_check(inter, grad_y, out)
     tok_off, w_off = _meta(tok_off), _meta(w_off)
     TW, H = out.shape
+    ev = _ev_begin()
     rc = lib.moe_grouped_gemm_down_dw(
         ptr(inter), inter.shape[0], inter.stride(0), ptr(grad_y), grad_y.stride(0), H, TW,
         ptr(tok_off), ptr(w_off), int(num_experts), ptr(out), DTYPE_CODE[inter.dtype], int(tile_n),
         ptr(status_buffer(inter.device)), stream_handle(inter.device),
     )
+    _ev_end(ev, "grouped_gemm_down_dw")
     check(rc, "moe_grouped_gemm_down_dw")
+    _count(1)
     return out

@@ -1,0 +1,363 @@
+"""Mixture-of-experts MLP layer on the sm_100a kernels of this package.
+
+Drop-in for triton_moe/moe.py: `TritonMoEConfig` (:30-39) and `TritonMoEMLP`
+(:42-518) keep their names, constructor, parameters (`router.weight`, `w1`,
+`w2`: identical state_dict keys and layouts), buffers, `forward`,
+`forward_with_intermediates` and `forward_profiled`.
+
+The training path differs from the reference in how it is executed, not in
+what it computes:
+  * the layer body after routing (route -> gather -> up(relu^2) -> down ->
+    combine, and the mirrored backward) is one autograd Function that calls
+    the C-ABI kernels directly;
+  * every token-space buffer is sized by the worst-case padded row count
+    (assignments + experts * (block_size - 1)), and every kernel reads the
+    actual per-expert extents from device memory, so the forward and the
+    backward never synchronise with the host and can be captured in a CUDA
+    graph;
+  * the relu^2 derivative is fused into the epilogue of the down-projection's
+    dIntermediate GEMM, and the unit-weight scatter of the gather backward is
+    the same single-pass combine kernel as the forward scatter.
+Numerics follow the reference's rounding points (fp32 accumulation, relu^2
+applied in fp32 before the store, derivative computed in fp32 and rounded
+before the dX / dW GEMMs).  As in the reference, the routing weights receive
+no gradient from the layer output (scatter.py:160-176).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.autograd.function import once_differentiable
+
+from .kernels import (
+    _ops,
+    fused_route,
+    grouped_gemm_down,
+    grouped_gemm_up,
+    padded_gather,
+    padded_scatter,
+)
+
+
+@dataclass
+class TritonMoEConfig:
+    """Configuration of the MoE layer (same fields as triton_moe.TritonMoEConfig)."""
+
+    n_embd: int = 768
+    expert_sizes: list = field(default_factory=lambda: [(64, 256)])
+    num_active_experts: int = 8
+    norm_topk_prob: bool = True
+    block_size: int = 64
+    use_megablocks_gather_scatter: bool = False
+
+
+@dataclass
+class _Plan:
+    """Static per-layer launch plan (host constants + device offset table)."""
+
+    num_experts: int
+    top_k: int
+    block_size: int
+    hidden: int
+    max_width: int
+    w_off: torch.Tensor  # [E+1] int32, device
+    tile_n_width: int  # N tile for GEMMs whose N is an expert width
+    tile_n_hidden: int  # N tile for GEMMs whose N is the hidden size
+
+
+class _MoEMLPFunction(torch.autograd.Function):
+    """route -> gather -> up(relu^2) -> down -> combine, and the backward."""
+
+    @staticmethod
+    def forward(ctx, x_flat, w1, w2, weights, selected, plan: _Plan):
+        T, H = x_flat.shape
+        E, k = plan.num_experts, plan.top_k
+        r = _ops.route(selected, E, plan.block_size, "up")
+        cap = r.p_capacity
+        rows = max(cap, 1)
+        p_dev = r.expert_token_offsets[E:]  # device scalar: padded row count
+        dev, dt = x_flat.device, x_flat.dtype
+        train = any(ctx.needs_input_grad[:3])
+
+        xg = torch.empty(rows, H, device=dev, dtype=dt)
+        _ops.gather(x_flat, r.row_to_assignment, k, cap, out=xg, rows_device=p_dev)
+        h = torch.empty(rows, plan.max_width, device=dev, dtype=dt)
+        pre = torch.empty_like(h) if train else None
+        _ops.gemm_up(xg, w1, r.expert_token_offsets, plan.w_off, None, E, "relu_squared", h, pre,
+                     tile_n=plan.tile_n_width)
+        y = torch.empty(rows, H, device=dev, dtype=dt)
+        _ops.gemm_down(h, w2, r.expert_token_offsets, plan.w_off, None, E, y,
+                       tile_n=plan.tile_n_hidden)
+        out = _ops.combine(y, r.assignment_to_row, T, k, weights=weights)
+
+        if train:
+            ctx.save_for_backward(xg, h, pre, weights, w1, w2, r.row_to_assignment,
+                                  r.assignment_to_row, r.expert_token_offsets)
+            ctx.plan = plan
+            ctx.cap = cap
+            ctx.T = T
+        ctx.mark_non_differentiable(r.tokens_per_expert)
+        return out, r.tokens_per_expert
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_out, _grad_tpe):
+        xg, h, pre, weights, w1, w2, r2a, a2r, tok_off = ctx.saved_tensors
+        plan = ctx.plan
+        E, k, cap = plan.num_experts, plan.top_k, ctx.cap
+        rows = max(cap, 1)
+        p_dev = tok_off[E:]
+        dev, dt = xg.device, xg.dtype
+        H = xg.shape[1]
+        grad_out = grad_out.to(dt)
+
+        # scatter backward: weighted gather of the output gradient
+        gy = torch.empty(rows, H, device=dev, dtype=dt)
+        _ops.gather(grad_out, r2a, k, cap, out=gy, rows_device=p_dev, weights=weights)
+        # down backward: dIntermediate with the relu^2 derivative fused, then dW2
+        dact = torch.empty(rows, plan.max_width, device=dev, dtype=dt)
+        _ops.gemm_down_dinter(gy, w2, tok_off, plan.w_off, None, E, dact, pre_act=pre,
+                              tile_n=plan.tile_n_width)
+        gw2 = torch.empty_like(w2) if ctx.needs_input_grad[2] else None
+        if gw2 is not None:
+            _ops.gemm_down_dw(h, gy, tok_off, plan.w_off, E, gw2, tile_n=plan.tile_n_hidden)
+        # up backward: dX (gathered space) and dW1
+        gx = None
+        if ctx.needs_input_grad[0]:
+            gxg = torch.empty(rows, H, device=dev, dtype=dt)
+            _ops.gemm_up_dx(dact, w1, tok_off, plan.w_off, None, E, gxg,
+                            tile_n=plan.tile_n_hidden)
+            # gather backward: unit-weight combine of the k copies of each token
+            gx = _ops.combine(gxg, a2r, ctx.T, k, weights=None)
+        gw1 = None
+        if ctx.needs_input_grad[1]:
+            gw1 = torch.empty_like(w1)
+            _ops.gemm_up_dw(xg, dact, tok_off, plan.w_off, E, gw1, tile_n=plan.tile_n_width)
+        return gx, gw1, gw2, None, None, None
+
+
+class TritonMoEMLP(nn.Module):
+    """Mixture-of-experts MLP with variable-width experts (drop-in for
+    triton_moe.TritonMoEMLP)."""
+
+    def __init__(self, config: TritonMoEConfig):
+        super().__init__()
+        self.config = config
+        self.num_experts = sum(count for count, _ in config.expert_sizes)
+        self.num_active_experts = config.num_active_experts
+        self.norm_topk_prob = config.norm_topk_prob
+        self.block_size = config.block_size
+
+        self.expert_widths = []
+        self.expert_offsets = [0]
+        for count, size in config.expert_sizes:
+            assert size % self.block_size == 0, (
+                f"expert sizes must be divisible by {self.block_size}"
+            )
+            for _ in range(count):
+                self.expert_widths.append(size)
+                self.expert_offsets.append(self.expert_offsets[-1] + size)
+        self.total_expert_width = self.expert_offsets[-1]
+        self.max_expert_width = max(self.expert_widths)
+
+        self.router = nn.Linear(config.n_embd, self.num_experts, bias=False)
+        self.w1 = nn.Parameter(torch.empty(config.n_embd, self.total_expert_width))
+        self.w2 = nn.Parameter(torch.empty(self.total_expert_width, config.n_embd))
+        nn.init.trunc_normal_(self.w1, mean=0.0, std=0.02, a=-0.06, b=0.06)
+        nn.init.trunc_normal_(self.w2, mean=0.0, std=0.02, a=-0.06, b=0.06)
+
+        self.register_buffer("expert_widths_t", torch.tensor(self.expert_widths, dtype=torch.int32),
+                             persistent=False)
+        self.register_buffer("expert_weight_offsets_t",
+                             torch.tensor(self.expert_offsets, dtype=torch.int32), persistent=False)
+
+        mean_w = sum(self.expert_widths) / self.num_experts
+        self.register_buffer(
+            "expert_widths_normalized",
+            torch.tensor([w / mean_w for w in self.expert_widths], dtype=torch.float32),
+            persistent=False,
+        )
+
+        # experts of a (count > 1) size class form a load-balance group; singleton
+        # classes are left out of the grouped loss (moe.py:108-146)
+        expert_to_group, group_sizes, gidx = [], [], 0
+        for count, _size in config.expert_sizes:
+            expert_to_group += [gidx if count > 1 else -1] * count
+            if count > 1:
+                group_sizes.append(count)
+                gidx += 1
+        self._num_valid_groups = len(group_sizes)
+        self._all_experts_valid = all(g >= 0 for g in expert_to_group)
+        if self._num_valid_groups > 0:
+            membership = torch.zeros(self.num_experts, self._num_valid_groups)
+            for i, g in enumerate(expert_to_group):
+                if g >= 0:
+                    membership[i, g] = 1.0
+            self.register_buffer("group_membership", membership, persistent=False)
+            self.register_buffer("group_sizes", torch.tensor(group_sizes, dtype=torch.float32),
+                                 persistent=False)
+            self.register_buffer(
+                "valid_expert_indices",
+                torch.tensor([i for i, g in enumerate(expert_to_group) if g >= 0],
+                             dtype=torch.long),
+                persistent=False,
+            )
+        else:
+            self.register_buffer("group_membership", torch.empty(0), persistent=False)
+            self.register_buffer("group_sizes", torch.tensor([1.0]), persistent=False)
+            self.register_buffer("valid_expert_indices", torch.empty(0, dtype=torch.long),
+                                 persistent=False)
+        self._plan_cache: _Plan | None = None
+
+    # ------------------------------------------------------------------ helpers
+    def _plan(self) -> _Plan:
+        p = self._plan_cache
+        w_off = self.expert_weight_offsets_t
+        if p is None or p.w_off is not w_off:
+            tn_w = 256 if all(w % 256 == 0 for w in self.expert_widths) else 128
+            tn_h = 256 if self.config.n_embd % 256 == 0 else 128
+            p = _Plan(self.num_experts, self.num_active_experts, self.block_size,
+                      self.config.n_embd, self.max_expert_width, w_off, tn_w, tn_h)
+            self._plan_cache = p
+        return p
+
+    def _route_weights(self, x_flat):
+        router_logits = self.router(x_flat)
+        router_probs = F.sigmoid(router_logits.float())
+        top_k_weights, selected_experts = torch.topk(router_probs, self.num_active_experts, dim=-1)
+        if self.norm_topk_prob:
+            top_k_weights = top_k_weights / (top_k_weights.sum(dim=-1, keepdim=True) + 1e-20)
+        top_k_weights = top_k_weights.to(x_flat.dtype)
+        return router_logits, router_probs, top_k_weights, selected_experts
+
+    def _aux_losses(self, router_logits, router_probs, tokens_per_expert, dtype):
+        router_z_loss = torch.logsumexp(router_logits, dim=-1).pow(2).mean()
+        f_i = (tokens_per_expert.float() / tokens_per_expert.sum()).to(dtype)
+        load_balance_loss = self._compute_load_balance_loss(router_probs, f_i)
+        compute_loss = (router_probs @ self.expert_widths_normalized.to(router_probs.dtype)).mean()
+        aux = {
+            "router_z_loss": router_z_loss,
+            "load_balance_loss": load_balance_loss,
+            "compute_loss": compute_loss,
+        }
+        return aux, f_i
+
+    # ------------------------------------------------------------------ forward
+    @torch.compiler.disable
+    def forward(self, x: torch.Tensor):
+        """x: [batch, seq, n_embd] -> (output, aux_loss dict, f_i)."""
+        batch_size, seq_len, n_embd = x.shape
+        x_flat = x.reshape(batch_size * seq_len, n_embd)
+        router_logits, router_probs, top_k_weights, selected = self._route_weights(x_flat)
+        out_flat, tokens_per_expert = _MoEMLPFunction.apply(
+            x_flat.to(self.w1.dtype), self.w1, self.w2, top_k_weights.reshape(-1),
+            selected.reshape(-1), self._plan(),
+        )
+        output = out_flat.reshape(batch_size, seq_len, -1)
+        aux, f_i = self._aux_losses(router_logits, router_probs, tokens_per_expert, x.dtype)
+        return output, aux, f_i
+
+    def _compute_load_balance_loss(self, router_probs: torch.Tensor, f_i: torch.Tensor) -> torch.Tensor:
+        """Load-balance loss within expert size groups (moe.py:276-303)."""
+        p_i = router_probs.mean(dim=0)
+        if len(set(self.expert_widths)) == 1:
+            return self.num_experts * (f_i.float() @ p_i.float())
+        if self._num_valid_groups == 0:
+            return f_i.float() @ p_i.float()
+        fi_pi = f_i.float() * p_i.float()
+        membership = self.group_membership.to(fi_pi.dtype)
+        if self._all_experts_valid:
+            group_sums = fi_pi @ membership
+        else:
+            group_sums = fi_pi.index_select(0, self.valid_expert_indices) @ membership.index_select(
+                0, self.valid_expert_indices)
+        return (self.group_sizes.to(fi_pi.dtype) * group_sums).mean()
+
+    def _offsets(self, padded_bins, device):
+        expert_token_offsets = torch.cat(
+            [torch.zeros(1, device=device, dtype=torch.int32), padded_bins])
+        padded_tokens_per_expert = torch.cat([padded_bins[:1], padded_bins[1:] - padded_bins[:-1]])
+        return expert_token_offsets, padded_tokens_per_expert
+
+    def forward_with_intermediates(self, x: torch.Tensor) -> dict[str, Any]:
+        """Forward returning every intermediate in the reference layout (moe.py:305-409)."""
+        batch_size, seq_len, n_embd = x.shape
+        x_flat = x.reshape(batch_size * seq_len, n_embd)
+        router_logits, router_probs, top_k_weights, selected_experts = self._route_weights(x_flat)
+        top_k_weights_flat = top_k_weights.reshape(-1)
+        selected_experts_flat = selected_experts.reshape(-1)
+        bin_ids, indices, tokens_per_expert, bins, padded_bins = fused_route(
+            selected_experts_flat, self.num_experts, block_size=self.block_size, rounding="up")
+        expert_token_offsets, padded_tokens_per_expert = self._offsets(padded_bins, x.device)
+        x_gathered = padded_gather(x_flat, indices, bin_ids, bins, padded_bins,
+                                   self.num_active_experts)
+        x_up = grouped_gemm_up(x_gathered.to(self.w1.dtype), self.w1, expert_token_offsets,
+                               self.expert_weight_offsets_t, self.expert_widths_t,
+                               padded_tokens_per_expert, self.max_expert_width,
+                               activation="relu_squared")
+        x_down = grouped_gemm_down(x_up, self.w2, expert_token_offsets,
+                                   self.expert_weight_offsets_t, self.expert_widths_t,
+                                   padded_tokens_per_expert, self.config.n_embd)
+        output_flat = padded_scatter(x_down, indices, bin_ids, top_k_weights_flat, bins,
+                                     padded_bins, self.num_active_experts)
+        output = output_flat.reshape(batch_size, seq_len, -1)
+        return {
+            "output": output,
+            "x_flat": x_flat,
+            "router_logits": router_logits,
+            "router_probs": router_probs,
+            "top_k_weights": top_k_weights,
+            "top_k_weights_flat": top_k_weights_flat,
+            "selected_experts": selected_experts,
+            "selected_experts_flat": selected_experts_flat,
+            "bin_ids": bin_ids,
+            "indices": indices,
+            "tokens_per_expert": tokens_per_expert,
+            "bins": bins,
+            "padded_bins": padded_bins,
+            "x_gathered": x_gathered,
+            "x_after_up": x_up,
+            "x_after_down": x_down,
+            "x_scattered": output_flat,
+        }
+
+    def forward_profiled(self, x: torch.Tensor, profiler):
+        """Forward with per-step timing through `profiler.step(name)` context
+        managers, with the reference's step names (moe.py:411-518)."""
+        batch_size, seq_len, n_embd = x.shape
+        with profiler.step("flatten"):
+            x_flat = x.reshape(batch_size * seq_len, n_embd)
+        with profiler.step("routing"):
+            router_logits, router_probs, top_k_weights, selected_experts = self._route_weights(x_flat)
+            top_k_weights_flat = top_k_weights.reshape(-1)
+            selected_experts_flat = selected_experts.reshape(-1)
+        with profiler.step("fused_route"):
+            bin_ids, indices, tokens_per_expert, bins, padded_bins = fused_route(
+                selected_experts_flat, self.num_experts, block_size=self.block_size,
+                rounding="up")
+            expert_token_offsets, padded_tokens_per_expert = self._offsets(padded_bins, x.device)
+        with profiler.step("gather"):
+            x_gathered = padded_gather(x_flat, indices, bin_ids, bins, padded_bins,
+                                       self.num_active_experts)
+        with profiler.step("gemm_up"):
+            x_up = grouped_gemm_up(x_gathered.to(self.w1.dtype), self.w1, expert_token_offsets,
+                                   self.expert_weight_offsets_t, self.expert_widths_t,
+                                   padded_tokens_per_expert, self.max_expert_width,
+                                   activation="relu_squared")
+        with profiler.step("gemm_down"):
+            x_down = grouped_gemm_down(x_up, self.w2, expert_token_offsets,
+                                       self.expert_weight_offsets_t, self.expert_widths_t,
+                                       padded_tokens_per_expert, self.config.n_embd)
+        with profiler.step("scatter"):
+            output_flat = padded_scatter(x_down, indices, bin_ids, top_k_weights_flat, bins,
+                                         padded_bins, self.num_active_experts)
+        with profiler.step("reshape"):
+            output = output_flat.reshape(batch_size, seq_len, -1)
+        with profiler.step("aux_loss"):
+            aux, f_i = self._aux_losses(router_logits, router_probs, tokens_per_expert, x.dtype)
+        return output, aux, f_i
