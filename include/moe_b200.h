@@ -83,6 +83,34 @@ MOE_API int moe_route(const void* selected_experts, int selected_is_int64, int64
               void* workspace, int64_t workspace_bytes, int* status, void* stream);
 
 /*
+ * moe_route without a workspace argument.  This entry point has no
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory themselves -- a plain C or FFI caller that only holds the
+ * buffers it was handed, a runtime whose pool or caching allocator already
+ * owns the GPU's memory (so an extra cudaMalloc can fail or fragment it), or
+ * a latency-critical loop where cudaMalloc/cudaFree would synchronise the
+ * device.  It allocates nothing: the histogram scratch is a fixed 256 KiB
+ * array of device memory inside the library (room for the largest scratch
+ * moe_route can need: 256 units x 256 experts x 4 bytes), held by every GPU
+ * that loads the library until the process exits.  Limits are those of
+ * moe_route (num_experts <= 256); a problem whose scratch would exceed the
+ * array is rejected with MOE_ERR_CAPACITY.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current);
+ * make that first call before any stream capture.  All calls on a device share
+ * the array and it keeps the last call's contents (nothing in it needs to
+ * start at zero), so calls whose kernels overlap on the same GPU -- e.g. on
+ * two streams -- race on it and must be serialised by the caller.  Outputs and
+ * their meaning are exactly those of moe_route.
+ */
+MOE_API int moe_route_no_alloc(const void* selected_experts, int selected_is_int64,
+                               int64_t num_assignments, int num_experts, int block_size,
+                               int rounding, int32_t* bin_ids, int32_t* indices,
+                               int32_t* tokens_per_expert, int32_t* bins, int32_t* padded_bins,
+                               int32_t* expert_token_offsets, int32_t* padded_tokens_per_expert,
+                               int32_t* row_to_assignment, int64_t padded_capacity,
+                               int32_t* assignment_to_row, int* status, void* stream);
+
+/*
  * Padded-row maps from the reference's sorted-order metadata (indices,
  * bin_ids, bins, padded_bins as returned by fused_route).  The row arithmetic
  * is that of _padded_gather_kernel (triton_moe/kernels/gather.py:29-50).

@@ -16,6 +16,10 @@ int route(const void* sel, int sel_is_int64, long long A, int E, int bs, int mod
           int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins, int32_t* padded_bins,
           int32_t* tok_off, int32_t* ptpe, int32_t* row_asg, long long p_cap, int32_t* asg_row,
           void* ws, long long ws_bytes, int* status, cudaStream_t st);
+int route_static_scratch(const void* sel, int sel_is_int64, long long A, int E, int bs, int mode,
+                         int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins,
+                         int32_t* padded_bins, int32_t* tok_off, int32_t* ptpe, int32_t* row_asg,
+                         long long p_cap, int32_t* asg_row, int* status, cudaStream_t st);
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
                 long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
                 int dtype, cudaStream_t st);
@@ -98,6 +102,22 @@ int moe_route(const void* selected_experts, int selected_is_int64, int64_t num_a
                     expert_token_offsets, padded_tokens_per_expert, row_to_assignment,
                     padded_capacity, assignment_to_row, workspace, workspace_bytes, status,
                     S(stream));
+}
+
+// Same routing as moe_route, for callers that cannot allocate device memory:
+// the histogram scratch lives in a fixed device array inside the library.
+int moe_route_no_alloc(const void* selected_experts, int selected_is_int64,
+                       int64_t num_assignments, int num_experts, int block_size, int rounding,
+                       int32_t* bin_ids, int32_t* indices, int32_t* tokens_per_expert,
+                       int32_t* bins, int32_t* padded_bins, int32_t* expert_token_offsets,
+                       int32_t* padded_tokens_per_expert, int32_t* row_to_assignment,
+                       int64_t padded_capacity, int32_t* assignment_to_row, int* status,
+                       void* stream) {
+  return moe::route_static_scratch(selected_experts, selected_is_int64, num_assignments,
+                                   num_experts, block_size, rounding, bin_ids, indices,
+                                   tokens_per_expert, bins, padded_bins, expert_token_offsets,
+                                   padded_tokens_per_expert, row_to_assignment, padded_capacity,
+                                   assignment_to_row, status, S(stream));
 }
 
 int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "moe_internal.h"
 
@@ -276,6 +277,60 @@ int route(const void* sel, int sel_is_int64, long long A, int E, int bs, int mod
   if (sel_is_int64)
     return route_impl(static_cast<const long long*>(sel), A, E, bs, mode, o, ws, ws_bytes, st);
   return route_impl(static_cast<const int32_t*>(sel), A, E, bs, mode, o, ws, ws_bytes, st);
+}
+
+// ---- routing without caller-provided scratch ------------------------------------
+// The per-unit histogram workspace normally comes from the caller.  This
+// variant keeps it in a file-scope device array instead, so it can serve
+// callers that cannot allocate device memory.  The array is sized for the
+// largest workspace route() can ask for (at most 256 units x 256 experts of
+// int32 = 256 KiB); every GPU that loads the library holds it until exit.
+// Nothing in it has to start at zero: the count phase writes every entry the
+// later phases read.  Every call on a device shares that device's copy and it
+// keeps the last call's contents, so two calls whose kernels overlap on the
+// same GPU (e.g. issued on different streams) race on it.
+namespace {
+constexpr long long kRouteScratchInts = 256LL * kMaxE;
+constexpr int kMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) int32_t g_route_scratch[kRouteScratchInts];
+
+// Device address of g_route_scratch on the current device.  Host code cannot
+// use the array's name as a device pointer, so the address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+static void* route_scratch_address(int* err) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *err = kStatusCuda;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || p == nullptr) {
+      *err = kStatusCuda;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+int route_static_scratch(const void* sel, int sel_is_int64, long long A, int E, int bs, int mode,
+                         int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins,
+                         int32_t* padded_bins, int32_t* tok_off, int32_t* ptpe, int32_t* row_asg,
+                         long long p_cap, int32_t* asg_row, int* status, cudaStream_t st) {
+  if (E <= 0 || E > kMaxE || A < 0) return kStatusBadArg;
+  const long long need = route_workspace_bytes(A, E);
+  if (need > kRouteScratchInts * 4) return kStatusCapacity;
+  int err = kStatusOk;
+  void* ws = route_scratch_address(&err);
+  if (ws == nullptr) return err;
+  return route(sel, sel_is_int64, A, E, bs, mode, bin_ids, indices, tpe, bins, padded_bins,
+               tok_off, ptpe, row_asg, p_cap, asg_row, ws, need, status, st);
 }
 
 }  // namespace moe

@@ -41,6 +41,7 @@ _SIGS = {
     "moe_status_string": [_I],
     "moe_route_workspace_bytes": [_L, _I],
     "moe_route": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _P, _P],
+    "moe_route_no_alloc": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P],
     "moe_build_row_map": [_P, _P, _P, _P, _L, _L, _P, _L, _P, _P, _P],
     "moe_gather_map": [_P, _L, _I, _P, _P],
     "moe_padded_gather": [_P, _L, _L, _P, _I, _L, _P, _P, _P, _L, _I, _P],
@@ -55,7 +56,11 @@ _SIGS = {
     ],
     "moe_grouped_gemm_down_dw": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _I, _P, _I, _I, _P, _P],
 }
-_RESTYPE = {"moe_version": c_char_p, "moe_status_string": c_char_p, "moe_route_workspace_bytes": c_int64}
+_RESTYPE = {
+    "moe_version": c_char_p,
+    "moe_status_string": c_char_p,
+    "moe_route_workspace_bytes": c_int64,
+}
 
 EXPORTED = tuple(_SIGS)
 
