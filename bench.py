@@ -11,6 +11,9 @@ backward).  The default workload is BASELINE config 3, the north-star
 top-2, batch 8 x seq 1024 = 8192 tokens, bf16, x ~ N(0,1), weights N(0,0.02),
 router from a random-init linear.
 
+Execution: the layer never synchronises the host, so the step is captured once
+in a CUDA graph and replayed (the eager time is reported beside it).
+
 Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
 events on the launch stream, with a 256 MiB write between steps to flush the
 126 MB L2; barrier + synchronize on both sides; the per-rank time is the sum
@@ -259,6 +262,34 @@ def time_cpu_oracle(cfg, budget_s=15.0, tokens=None):
     return tokens / dt, tokens, reps
 
 
+def capture_step(layer, x, gout):
+    """Capture one fwd+bwd of the layer in a CUDA graph (the layer never
+    synchronises the host, so the whole step is capturable).  Returns the graph,
+    its static output and how many of our kernels one replay launches."""
+    import torch
+
+    from moe_b200.kernels import _ops
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            layer.zero_grad(set_to_none=True)
+            x.grad = None
+            out, _, _ = layer(x)
+            out.backward(gout)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    layer.zero_grad(set_to_none=True)
+    x.grad = None
+    graph = torch.cuda.CUDAGraph()
+    l0 = _ops.launch_count
+    with torch.cuda.graph(graph):
+        out, _, _ = layer(x)
+        out.backward(gout)
+    return graph, out, _ops.launch_count - l0
+
+
 # ------------------------------------------------------------------ arms
 def run_reference(args, cfg, name):
     ws, rank, _ = dist_env()
@@ -336,54 +367,71 @@ def run_b200(args, cfg, name):
     for _ in range(max(args.warmup, 3)):
         step(x, gout)
     torch.cuda.synchronize()
+    if args.profile_step:
+        # one eager step for an external profiler (ncu), nothing timed
+        step(x, gout)
+        torch.cuda.synchronize()
+        return 0
+
+    graph, out_static, per_step_launches = capture_step(layer, x, gout)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
 
     # clock samples: a ~1.5 s soak of the same step right before the timed loop
     sampler = ClockSampler(gpu_selector(dev))
     sampler.start()
     t_end = time.perf_counter() + 1.5
     while time.perf_counter() < t_end:
-        step(x, gout)
+        for _ in range(20):
+            graph.replay()
         torch.cuda.synchronize()
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    l0 = _ops.launch_count
-    for i in range(args.steps):
-        flush.zero_()  # 256 MiB write: evicts the 126 MB L2 between timed steps
-        starts[i].record()
-        step(x, gout)
-        ends[i].record()
-    torch.cuda.synchronize()
-    launches = _ops.launch_count - l0
-    if ws > 1:
-        dist.barrier()
+    def timed(fn, n):
+        """Sum of per-step device times (CUDA events on the launch stream), with a
+        256 MiB write between steps to evict the 126 MB L2; max over ranks."""
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(n):
+            flush.zero_()
+            starts[i].record()
+            fn()
+            ends[i].record()
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        tot = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+        t = torch.tensor([tot], device=dev, dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    job_ms = timed(graph.replay, args.steps)
     clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    job_ms = float(t.item())
+    launches = per_step_launches * args.steps
     ms_per_step = job_ms / args.steps
     value = T * ws * args.steps / (job_ms / 1e3)
+    eager_ms = timed(lambda: step(x, gout), args.steps) / args.steps
 
-    # grouped-GEMM roofline: per-launch CUDA events over instrumented steps
+    # per-kernel device time (CUDA events around each of our launches, eager steps)
     with torch.no_grad():
         _, _, _, sel = layer._route_weights(x.detach().reshape(-1, H))
         tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts).cpu().tolist()
     flops = gemm_flops(tpe, cfg)
     reps = 5
-    gemm_ms = 0.0
+    per_kind: dict[str, float] = {}
     for _ in range(reps):
         flush.zero_()
-        with _ops.record_gemm_events() as evs:
+        with _ops.record_kernel_events() as evs:
             step(x, gout)
         torch.cuda.synchronize()
-        gemm_ms += sum(s.elapsed_time(e) for _, s, e in evs)
-    gemm_ms /= reps
+        for kname, a, b in evs:
+            per_kind[kname] = per_kind.get(kname, 0.0) + a.elapsed_time(b) / reps
+    gemm_ms = sum(v for k, v in per_kind.items() if k.startswith("grouped_gemm"))
+    perm_ms = sum(v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
     n_gemm_launches = 6
     peak_tf, peak_hbm, peak_kind = measured_peaks()
     achieved = flops / (gemm_ms / 1e3) / 1e12
@@ -401,31 +449,31 @@ def run_b200(args, cfg, name):
         "avg_launch_ms": gemm_ms / n_gemm_launches,
         "traffic": (traffic_step / n_gemm_launches) if traffic_step else None,
     }
+    pbytes = permute_bytes(cfg)
+    permute = {
+        "kernels": "gather, combine, weighted gather, unit-weight combine (4 launches per step)",
+        "bound": "hbm",
+        "achieved": pbytes / (perm_ms / 1e3) / 1e9,
+        "peak": peak_hbm,
+        "unit": "GB/s",
+        "frac": pbytes / (perm_ms / 1e3) / 1e9 / peak_hbm,
+        "bytes_per_step": pbytes,
+        "ms_per_step": perm_ms,
+    }
+    kernel_us = {k: round(v * 1e3, 2) for k, v in sorted(per_kind.items())}
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers (graphed step)
     out_host = torch.empty(cfg["batch"], cfg["seq"], H, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x.detach())
-    gd = torch.empty_like(gout)
-    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        flush.zero_()
-        e_starts[i].record()
-        xd.copy_(x_host, non_blocking=True)
-        gd.copy_(g_host, non_blocking=True)
-        xi = xd.detach().requires_grad_(True)
-        out = step(xi, gd)
-        out_host.copy_(out.detach(), non_blocking=True)
-        e_ends[i].record()
-    torch.cuda.synchronize()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
-    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = T * ws * args.steps / (float(t.item()) / 1e3)
+
+    def e2e_step():
+        with torch.no_grad():
+            x.copy_(x_host, non_blocking=True)
+            gout.copy_(g_host, non_blocking=True)
+        graph.replay()
+        out_host.copy_(out_static.detach(), non_blocking=True)
+
+    e2e_ms = timed(e2e_step, args.steps)
+    e2e_value = T * ws * args.steps / (e2e_ms / 1e3)
     nbytes = x_host.numel() * 2
 
     cpu = None
@@ -457,8 +505,11 @@ def run_b200(args, cfg, name):
                 "l2": "flushed by a 256 MiB write between timed steps",
             },
             "roofline": roofline,
-            "gemm_frac_of_bf16_peak": roofline["frac"],
-            "permute_bytes_per_step": permute_bytes(cfg),
+            "permute_roofline": permute,
+            "kernel_us_per_step_eager": kernel_us,
+            "eager_ms_per_step": eager_ms,
+            "execution": "step captured once in a CUDA graph and replayed (eager time in "
+                         "eager_ms_per_step)",
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
                     "d2h_bytes_per_step": nbytes},
@@ -479,6 +530,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="run the warm-up steps plus one eager step, print nothing (for ncu)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.impl == "reference":

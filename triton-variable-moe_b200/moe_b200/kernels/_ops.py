@@ -30,7 +30,7 @@ _GEMM_DTYPES = (torch.bfloat16, torch.float16)
 _status_bufs: dict[int, torch.Tensor] = {}
 
 # Number of CUDA kernels launched through this module (host-side count; the
-# routing entry point launches three).  bench.py reports it per timed region.
+# routing entry point launches one or three).  bench.py reports it per timed region.
 launch_count = 0
 
 
@@ -39,23 +39,23 @@ def _count(n: int = 1) -> None:
     launch_count += n
 
 
-_gemm_events: list | None = None
+_kernel_events: list | None = None
 
 
 @contextmanager
-def record_gemm_events():
+def record_kernel_events():
     """Within the block, every grouped GEMM launch is bracketed by CUDA events
     on its launch stream; yields the list of (name, start, end) events."""
-    global _gemm_events
-    prev, _gemm_events = _gemm_events, []
+    global _kernel_events
+    prev, _kernel_events = _kernel_events, []
     try:
-        yield _gemm_events
+        yield _kernel_events
     finally:
-        _gemm_events = prev
+        _kernel_events = prev
 
 
 def _ev_begin():
-    if _gemm_events is None:
+    if _kernel_events is None:
         return None
     e = torch.cuda.Event(enable_timing=True)
     e.record()
@@ -66,7 +66,7 @@ def _ev_end(start, name: str) -> None:
     if start is not None:
         e = torch.cuda.Event(enable_timing=True)
         e.record()
-        _gemm_events.append((name, start, e))
+        _kernel_events.append((name, start, e))
 
 
 def status_buffer(device: torch.device) -> torch.Tensor:
@@ -137,14 +137,16 @@ def route(
     asg_row = torch.empty(max(A, 1), **i32) if want_rows else None
     ws_bytes = int(lib.moe_route_workspace_bytes(A, E))
     ws = torch.empty((ws_bytes + 3) // 4, **i32)
+    ev = _ev_begin()
     rc = lib.moe_route(
         ptr(sel), 1 if sel.dtype == torch.int64 else 0, A, E, int(block_size), ROUND_CODE[rounding],
         ptr(bin_ids), ptr(indices), ptr(tpe), ptr(bins), ptr(pbins), ptr(tok_off), ptr(ptpe),
         ptr(row_asg), cap, ptr(asg_row), ptr(ws), ws_bytes, ptr(status_buffer(dev)),
         stream_handle(dev),
     )
+    _ev_end(ev, "route")
     check(rc, "moe_route")
-    _count(3)
+    _count(1 if A <= 65536 else 3)  # one fused CTA for small problems
     return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
 
 
@@ -202,10 +204,12 @@ def gather(
         out = torch.empty(rows, H, dtype=x.dtype, device=x.device)
     if weights is not None:
         weights = weights.to(x.dtype).contiguous()
+    ev = _ev_begin()
     rc = lib.moe_padded_gather(
         ptr(x), x.stride(0), H, ptr(row_map), int(map_div), int(rows), ptr(rows_device),
         ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[x.dtype], stream_handle(x.device),
     )
+    _ev_end(ev, "gather" if weights is None else "weighted_gather")
     check(rc, "moe_padded_gather")
     _count(1)
     return out
@@ -228,10 +232,12 @@ def combine(
         out = torch.empty(num_tokens, H, dtype=y.dtype, device=y.device)
     if weights is not None:
         weights = weights.to(y.dtype).contiguous()
+    ev = _ev_begin()
     rc = lib.moe_padded_scatter(
         ptr(y), y.stride(0), H, ptr(assignment_to_row), int(num_tokens), int(top_k),
         ptr(weights), ptr(out), out.stride(0), DTYPE_CODE[y.dtype], stream_handle(y.device),
     )
+    _ev_end(ev, "combine")
     check(rc, "moe_padded_scatter")
     _count(1)
     return out
