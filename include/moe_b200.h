@@ -111,6 +111,18 @@ MOE_API int moe_route_no_alloc(const void* selected_experts, int selected_is_int
                                int32_t* assignment_to_row, int* status, void* stream);
 
 /*
+ * Top-k expert choice for the router output (triton_moe/moe.py:168-182):
+ * router_probs [num_tokens, num_experts] fp32 (sigmoid of the router logits)
+ * -> selected_experts [num_tokens, top_k] int32 in descending probability order
+ * (torch.topk; equal probabilities go to the lower expert index) and weights
+ * [num_tokens, top_k] = p / (sum_k p + 1e-20) when normalize, else p, rounded
+ * to weights_dtype.  num_experts <= 256, top_k <= 32.
+ */
+MOE_API int moe_router_topk(const float* router_probs, int64_t num_tokens, int num_experts,
+                            int top_k, int normalize, void* weights, int weights_dtype,
+                            int32_t* selected_experts, void* stream);
+
+/*
  * Padded-row maps from the reference's sorted-order metadata (indices,
  * bin_ids, bins, padded_bins as returned by fused_route).  The row arithmetic
  * is that of _padded_gather_kernel (triton_moe/kernels/gather.py:29-50).

@@ -23,7 +23,7 @@ INCLUDE = HERE.parent / "include"
 OBJ_DIR = HERE / "_build"
 OUT = HERE / "moe_b200" / "libmoe_b200.so"
 
-SOURCES = ["route.cu", "permute.cu", "grouped_gemm.cu", "capi.cu"]
+SOURCES = ["route.cu", "router.cu", "permute.cu", "grouped_gemm.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

@@ -20,6 +20,8 @@ int route_static_scratch(const void* sel, int sel_is_int64, long long A, int E, 
                          int32_t* bin_ids, int32_t* indices, int32_t* tpe, int32_t* bins,
                          int32_t* padded_bins, int32_t* tok_off, int32_t* ptpe, int32_t* row_asg,
                          long long p_cap, int32_t* asg_row, int* status, cudaStream_t st);
+int router_topk(const float* probs, long long T, int E, int k, int norm, void* w, int w_dtype,
+                int32_t* sel, cudaStream_t st);
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
                 long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
                 int dtype, cudaStream_t st);
@@ -118,6 +120,13 @@ int moe_route_no_alloc(const void* selected_experts, int selected_is_int64,
                                    tokens_per_expert, bins, padded_bins, expert_token_offsets,
                                    padded_tokens_per_expert, row_to_assignment, padded_capacity,
                                    assignment_to_row, status, S(stream));
+}
+
+int moe_router_topk(const float* router_probs, int64_t num_tokens, int num_experts, int top_k,
+                    int normalize, void* weights, int weights_dtype, int32_t* selected_experts,
+                    void* stream) {
+  return moe::router_topk(router_probs, num_tokens, num_experts, top_k, normalize, weights,
+                          weights_dtype, selected_experts, S(stream));
 }
 
 int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,

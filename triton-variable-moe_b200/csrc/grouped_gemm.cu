@@ -33,7 +33,9 @@ struct Cfg {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 1024;
+  static constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+  static constexpr int kSmemBytes =
+      1024 /*align slack*/ + kStages * kStageBytes + kEpiBytes + 256 /*barriers*/;
 };
 
 struct GroupTable {
@@ -117,7 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;                      // S stages of A
   uint8_t* sB = smem + S * C::kABytes;     // S stages of B
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint8_t* sEpi = smem + S * C::kStageBytes;  // epilogue staging, 4 KB per warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + C::kEpiBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* acc_full = bars + 2 * S;
@@ -154,6 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
     tc_fence_before();
   }
+  // Everything above touched only this CTA's own resources; from here on the
+  // kernel reads and writes global memory that earlier kernels in the stream
+  // produce or consume, so wait for them (programmatic dependent launch).
+  griddep_wait();
   if (warp == 2) {
     // Per-expert geometry and the tile prefix table: lane L owns a contiguous
     // chunk of experts, then a warp scan turns chunk sums into offsets.
@@ -200,6 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   tc_fence_after();
+  // The next kernel may start its own prologue now; it waits for this grid's
+  // completion before touching memory.
+  griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const int E = g.E;
   const int total = tb.prefix[E];
@@ -304,72 +314,134 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Results are
+    // produced one 64-column slab at a time: every lane converts its own row
+    // into a 32 x 128 B staging tile (16-byte chunks XOR-swizzled by row, so
+    // the row-per-lane writes and the row-major reads are bank-conflict free),
+    // then the warp stores the slab row-major, four full 128-byte rows per
+    // instruction.
+    const int q = warp & 3;
+    uint8_t* stg = sEpi + q * 4096;
     int buf = 0;
     uint32_t acc_phase = 0;
     T* D = reinterpret_cast<T*>(g.d);
     T* AUX = reinterpret_cast<T*>(g.aux);
+    const int rsub = lane >> 3;  // row within a 4-row group for the row-major phase
+    const int csub = lane & 7;   // 16-byte chunk within a 128-byte row
+    auto stg_chunk = [&](int row, int chunk) -> uint4* {
+      return reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4));
+    };
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int e, m0, n0;
       decode_tile<BN>(tb, E, t, e, m0, n0);
       const int M = tb.M[e], N = tb.N[e], K = tb.K[e];
       if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag)) break;
       tc_fence_after();
-      const int r = m0 + row_in_tile;
-      const bool row_ok = r < M;
-      const long long grow = static_cast<long long>(tb.dm[e]) + r;
+      const int rbase = m0 + q * 32;            // group row of this warp's first row
+      const int rows_ok = min(32, M - rbase);   // may be <= 0
+      const long long grow0 = static_cast<long long>(tb.dm[e]) + rbase;
       const int gcol0 = tb.dn[e] + n0;
       const int ncols = min(BN, N - n0);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      // row-major store of the staged slab (rows beyond the expert and columns
+      // beyond its width are skipped); all shared loads first, then the stores
+      auto store_slab = [&](T* dst, long long ld, int s, int cvalid) {
+        uint4 sv[8];
+#pragma unroll
+        for (int it = 0; it < 8; ++it) sv[it] = *stg_chunk(it * 4 + rsub, csub);
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int row = it * 4 + rsub;
+          if (row < rows_ok && csub * 8 < cvalid)
+            *reinterpret_cast<uint4*>(dst + (grow0 + row) * ld + gcol0 + s + csub * 8) = sv[it];
+        }
+      };
 #pragma unroll 1
-      for (int c = 0; c < ncols; c += 32) {
-        float v[32];
+      for (int s = 0; s < ncols; s += 64) {
+        const int cvalid = min(64, ncols - s);
+        float v[64];
         if (K > 0) {
-          tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                        static_cast<uint32_t>(buf * BN + c),
-                    v);
+          tmem_ld32(tbase + s, *reinterpret_cast<float(*)[32]>(&v[0]));
+          if (cvalid > 32) tmem_ld32(tbase + s + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int i = 0; i < 64; ++i) v[i] = 0.f;
         }
-        if (row_ok) {
-          T* drow = D + grow * g.ldd + gcol0 + c;
+        if constexpr (EPI == EPI_STORE) {
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            if (c + ch * 8 >= ncols) break;
+          for (int j = 0; j < 8; ++j) {
             uint4 o;
             uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-            if constexpr (EPI == EPI_STORE) {
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                op[i] = Cvt<T>::pack(v[ch * 8 + 2 * i], v[ch * 8 + 2 * i + 1]);
-            } else if constexpr (EPI == EPI_RELU2) {
-              uint4 p;
-              uint32_t* pp = reinterpret_cast<uint32_t*>(&p);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float a = fmaxf(v[ch * 8 + 2 * i], 0.f);
-                const float b = fmaxf(v[ch * 8 + 2 * i + 1], 0.f);
-                pp[i] = Cvt<T>::pack(a, b);
-                op[i] = Cvt<T>::pack(a * a, b * b);
-              }
-              *reinterpret_cast<uint4*>(AUX + grow * g.ld_aux + gcol0 + c + ch * 8) = p;
-            } else {  // EPI_DACT
-              const uint4 p =
-                  *reinterpret_cast<const uint4*>(AUX + grow * g.ld_aux + gcol0 + c + ch * 8);
-              const uint32_t* pp = reinterpret_cast<const uint32_t*>(&p);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                float p0, p1;
-                Cvt<T>::unpack(pp[i], p0, p1);
-                const float g0 = Cvt<T>::round(v[ch * 8 + 2 * i]);
-                const float g1 = Cvt<T>::round(v[ch * 8 + 2 * i + 1]);
-                op[i] = Cvt<T>::pack(p0 > 0.f ? g0 * 2.0f * p0 : 0.f,
-                                     p1 > 0.f ? g1 * 2.0f * p1 : 0.f);
-              }
-            }
-            *reinterpret_cast<uint4*>(drow + ch * 8) = o;
+            for (int i = 0; i < 4; ++i) op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
+            *stg_chunk(lane, j) = o;
           }
+          __syncwarp();
+          store_slab(D, g.ldd, s, cvalid);
+          __syncwarp();
+        } else if constexpr (EPI == EPI_RELU2) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 o;
+            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              v[j * 8 + 2 * i] = fmaxf(v[j * 8 + 2 * i], 0.f);
+              v[j * 8 + 2 * i + 1] = fmaxf(v[j * 8 + 2 * i + 1], 0.f);
+              op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
+            }
+            *stg_chunk(lane, j) = o;
+          }
+          __syncwarp();
+          store_slab(AUX, g.ld_aux, s, cvalid);
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 o;
+            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float a = v[j * 8 + 2 * i], b = v[j * 8 + 2 * i + 1];
+              op[i] = Cvt<T>::pack(a * a, b * b);
+            }
+            *stg_chunk(lane, j) = o;
+          }
+          __syncwarp();
+          store_slab(D, g.ldd, s, cvalid);
+          __syncwarp();
+        } else {  // EPI_DACT: stage pre (row-major, coalesced), combine per row
+          uint4 pv[8];  // all eight loads in flight before any shared store
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int row = it * 4 + rsub;
+            pv[it] = make_uint4(0, 0, 0, 0);
+            if (row < rows_ok && csub * 8 < cvalid)
+              pv[it] = __ldg(reinterpret_cast<const uint4*>(AUX + (grow0 + row) * g.ld_aux +
+                                                            gcol0 + s + csub * 8));
+          }
+#pragma unroll
+          for (int it = 0; it < 8; ++it) *stg_chunk(it * 4 + rsub, csub) = pv[it];
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 p = *stg_chunk(lane, j);
+            const uint32_t* pp = reinterpret_cast<const uint32_t*>(&p);
+            uint4 o;
+            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float p0, p1;
+              Cvt<T>::unpack(pp[i], p0, p1);
+              const float g0 = Cvt<T>::round(v[j * 8 + 2 * i]);
+              const float g1 = Cvt<T>::round(v[j * 8 + 2 * i + 1]);
+              op[i] = Cvt<T>::pack(p0 > 0.f ? g0 * 2.0f * p0 : 0.f, p1 > 0.f ? g1 * 2.0f * p1 : 0.f);
+            }
+            *stg_chunk(lane, j) = o;
+          }
+          __syncwarp();
+          store_slab(D, g.ldd, s, cvalid);
+          __syncwarp();
         }
       }
       tc_fence_before();
@@ -431,11 +503,25 @@ int launch_inst(const CUtensorMap& ta, const CUtensorMap& tbm, const GroupedGemm
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+            cudaSuccess)
       return kStatusCuda;
     attr_set[dev] = true;
   }
-  kern<<<grid, kThreads, smem, st>>>(ta, tbm, g);
+  // Programmatic dependent launch: this grid's prologue (barrier init, TMEM
+  // allocation, descriptor prefetch) overlaps the tail of the previous kernel.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tbm, g) != cudaSuccess) return kStatusCuda;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }
 

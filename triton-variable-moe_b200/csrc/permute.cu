@@ -74,96 +74,129 @@ struct V8<float> {
   static __device__ __forceinline__ float rnd(float v) { return v; }
 };
 
-constexpr int kRowsPerBlock = 8;  // one warp per row
+constexpr int kThreadsPerBlock = 256;
+
+// The permutation kernels are launched with programmatic dependent launch:
+// they wait for the previous grid before touching memory, and each block lets
+// the next grid start launching once it has finished its own work (the next
+// grid still waits for this one to complete before it touches memory).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_done() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // out[r, :] = src row map[r] / div of x (times w[map[r]] when w != null);
 // rows whose map entry is negative are zero.  Rows at or beyond *rows_dev
-// (when given) are not touched.
+// (when given) are not touched.  One thread per 8-element (16-byte) chunk.
 template <typename T, bool VEC>
-__global__ void gather_rows_kernel(const T* __restrict__ x, long long ldx, int H,
-                                   const int32_t* __restrict__ map, int div, long long rows,
-                                   const int32_t* __restrict__ rows_dev,
-                                   const T* __restrict__ w, T* __restrict__ out, long long ldo) {
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kThreadsPerBlock)
+    gather_rows_kernel(const T* __restrict__ x, long long ldx, int H,
+                       const int32_t* __restrict__ map, int div, long long rows,
+                       const int32_t* __restrict__ rows_dev, const T* __restrict__ w,
+                       T* __restrict__ out, long long ldo) {
+  pdl_wait();
   long long nrows = rows;
   if (rows_dev != nullptr) nrows = min(nrows, static_cast<long long>(*rows_dev));
-  for (long long r = static_cast<long long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
-       r < nrows; r += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
-    const int a = map[r];
-    T* orow = out + r * ldo;
-    if (a < 0) {
-      if constexpr (VEC) {
-        for (int c = lane * 8; c < H; c += 256) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-      } else {
-        for (int c = lane; c < H; c += 32) orow[c] = V8<T>::from_f(0.f);
-      }
-      continue;
-    }
-    const T* xrow = x + static_cast<long long>(a / div) * ldx;
+  constexpr int V = VEC ? 8 : 1;
+  const int per_row = (H + V - 1) / V;
+  const long long n = nrows * per_row;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / per_row;
+    const int c = static_cast<int>(i - r * per_row) * V;
+    const int a = __ldg(map + r);
+    T* o = out + r * ldo + c;
     if constexpr (VEC) {
-      if (w == nullptr) {
-        for (int c = lane * 8; c < H; c += 256)
-          *reinterpret_cast<uint4*>(orow + c) = __ldg(reinterpret_cast<const uint4*>(xrow + c));
+      if (a < 0) {
+        *reinterpret_cast<uint4*>(o) = make_uint4(0, 0, 0, 0);
       } else {
-        const float s = V8<T>::to_f(w[a]);
-        for (int c = lane * 8; c < H; c += 256) {
+        const uint4 u =
+            __ldg(reinterpret_cast<const uint4*>(x + static_cast<long long>(a / div) * ldx + c));
+        if (w == nullptr) {
+          *reinterpret_cast<uint4*>(o) = u;
+        } else {
           float f[8];
-          V8<T>::load(__ldg(reinterpret_cast<const uint4*>(xrow + c)), f);
+          V8<T>::load(u, f);
+          const float sc = V8<T>::to_f(w[a]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] *= s;
-          *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(f);
+          for (int k = 0; k < 8; ++k) f[k] *= sc;
+          *reinterpret_cast<uint4*>(o) = V8<T>::store(f);
         }
       }
     } else {
-      const float s = w ? V8<T>::to_f(w[a]) : 1.f;
-      for (int c = lane; c < H; c += 32)
-        orow[c] = w ? V8<T>::from_f(V8<T>::to_f(xrow[c]) * s) : xrow[c];
+      if (a < 0) {
+        *o = V8<T>::from_f(0.f);
+      } else {
+        const T v = x[static_cast<long long>(a / div) * ldx + c];
+        *o = w ? V8<T>::from_f(V8<T>::to_f(v) * V8<T>::to_f(w[a])) : v;
+      }
     }
   }
+  pdl_done();
 }
 
-// out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding)
-template <typename T, bool VEC>
-__global__ void combine_kernel(const T* __restrict__ y, long long ldy, int H,
-                               const int32_t* __restrict__ asg_row, long long T_tokens, int k,
-                               const T* __restrict__ w, T* __restrict__ out, long long ldo) {
-  const int lane = threadIdx.x & 31;
-  for (long long t = static_cast<long long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
-       t < T_tokens; t += static_cast<long long>(gridDim.x) * kRowsPerBlock) {
-    const int32_t* rows = asg_row + t * k;
-    T* orow = out + t * ldo;
-    if constexpr (VEC) {
-      for (int c = lane * 8; c < H; c += 256) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < k; ++j) {
-          const int row = rows[j];
-          if (row < 0) continue;
-          float f[8];
-          V8<T>::load(__ldg(reinterpret_cast<const uint4*>(y + row * ldy + c)), f);
-          if (w != nullptr) {
-            const float s = V8<T>::to_f(w[t * k + j]);
+// out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding).
+// One thread per 8-element chunk of a token; the k source rows are loaded
+// independently so their latencies overlap.
+template <typename T, bool VEC, int kMaxK>
+__global__ void __launch_bounds__(kThreadsPerBlock)
+    combine_kernel(const T* __restrict__ y, long long ldy, int H,
+                   const int32_t* __restrict__ asg_row, long long T_tokens, int k,
+                   const T* __restrict__ w, T* __restrict__ out, long long ldo) {
+  pdl_wait();
+  constexpr int V = VEC ? 8 : 1;
+  const int per_row = (H + V - 1) / V;
+  const long long n = T_tokens * per_row;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long t = i / per_row;
+    const int c = static_cast<int>(i - t * per_row) * V;
+    float acc[V];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += V8<T>::rnd(f[i] * s);
+    for (int q = 0; q < V; ++q) acc[q] = 0.f;
+    for (int j0 = 0; j0 < k; j0 += kMaxK) {
+      const int kk = min(kMaxK, k - j0);
+      int rows[kMaxK];
+      float sc[kMaxK];
+#pragma unroll
+      for (int j = 0; j < kMaxK; ++j) {
+        rows[j] = j < kk ? __ldg(asg_row + t * k + j0 + j) : -1;
+        sc[j] = (j < kk && w != nullptr) ? V8<T>::to_f(w[t * k + j0 + j]) : 1.f;
+      }
+      if constexpr (VEC) {
+        uint4 u[kMaxK];
+#pragma unroll
+        for (int j = 0; j < kMaxK; ++j)
+          if (rows[j] >= 0) u[j] = __ldg(reinterpret_cast<const uint4*>(y + rows[j] * ldy + c));
+#pragma unroll
+        for (int j = 0; j < kMaxK; ++j) {
+          if (rows[j] < 0) continue;
+          float f[8];
+          V8<T>::load(u[j], f);
+          if (w != nullptr) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[q] += V8<T>::rnd(f[q] * sc[j]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += f[i];
+            for (int q = 0; q < 8; ++q) acc[q] += f[q];
           }
         }
-        *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(acc);
-      }
-    } else {
-      for (int c = lane; c < H; c += 32) {
-        float acc = 0.f;
-        for (int j = 0; j < k; ++j) {
-          const int row = rows[j];
-          if (row < 0) continue;
-          const float v = V8<T>::to_f(y[row * ldy + c]);
-          acc += w ? V8<T>::rnd(v * V8<T>::to_f(w[t * k + j])) : v;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kMaxK; ++j) {
+          if (rows[j] < 0) continue;
+          const float v = V8<T>::to_f(y[rows[j] * ldy + c]);
+          acc[0] += (w != nullptr) ? V8<T>::rnd(v * sc[j]) : v;
         }
-        orow[c] = V8<T>::from_f(acc);
       }
     }
+    if constexpr (VEC) {
+      *reinterpret_cast<uint4*>(out + t * ldo + c) = V8<T>::store(acc);
+    } else {
+      out[t * ldo + c] = V8<T>::from_f(acc[0]);
+    }
   }
+  pdl_done();
 }
 
 // grad_act = pre > 0 ? round(g * 2 * pre) : 0, elementwise over [rows, cols].
@@ -216,7 +249,7 @@ __global__ void gather_map_kernel(const int32_t* __restrict__ row_asg, long long
 
 int grid_for(long long work_items, int per_block) {
   long long b = (work_items + per_block - 1) / per_block;
-  const long long cap = static_cast<long long>(num_sms()) * 16;
+  const long long cap = static_cast<long long>(num_sms()) * 64;
   if (b > cap) b = cap;
   if (b < 1) b = 1;
   return static_cast<int>(b);
@@ -224,45 +257,67 @@ int grid_for(long long work_items, int per_block) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+template <typename Kern, typename... Args>
+int launch_pdl(Kern kern, int grid, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreadsPerBlock);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) return kStatusCuda;
+  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
 template <typename T>
 int gather_t(const void* x, long long ldx, int H, const int32_t* map, int div, long long rows,
              const int32_t* rows_dev, const void* w, void* out, long long ldo, cudaStream_t st) {
-  if (rows <= 0) return kStatusOk;
-  const int grid = grid_for(rows, kRowsPerBlock);
+  if (rows <= 0 || H <= 0) return kStatusOk;
   const bool vec = H % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && aligned16(x) && aligned16(out);
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  T* op = static_cast<T*>(out);
   if constexpr (sizeof(T) == 2) {
-    if (vec) {
-      gather_rows_kernel<T, true><<<grid, kRowsPerBlock * 32, 0, st>>>(
-          static_cast<const T*>(x), ldx, H, map, div, rows, rows_dev, static_cast<const T*>(w),
-          static_cast<T*>(out), ldo);
-      return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
-    }
+    if (vec)
+      return launch_pdl(gather_rows_kernel<T, true>, grid_for(rows * (H / 8), kThreadsPerBlock),
+                        st, xp, ldx, H, map, div, rows, rows_dev, wp, op, ldo);
   }
-  gather_rows_kernel<T, false><<<grid, kRowsPerBlock * 32, 0, st>>>(
-        static_cast<const T*>(x), ldx, H, map, div, rows, rows_dev, static_cast<const T*>(w),
-        static_cast<T*>(out), ldo);
-  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+  return launch_pdl(gather_rows_kernel<T, false>, grid_for(rows * H, kThreadsPerBlock), st, xp,
+                    ldx, H, map, div, rows, rows_dev, wp, op, ldo);
 }
 
 template <typename T>
 int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long long T_tokens,
               int k, const void* w, void* out, long long ldo, cudaStream_t st) {
-  if (T_tokens <= 0) return kStatusOk;
-  const int grid = grid_for(T_tokens, kRowsPerBlock);
+  if (T_tokens <= 0 || H <= 0) return kStatusOk;
   const bool vec = H % 8 == 0 && ldy % 8 == 0 && ldo % 8 == 0 && aligned16(y) && aligned16(out);
-  if constexpr (sizeof(T) == 2) {
-    if (vec) {
-      combine_kernel<T, true><<<grid, kRowsPerBlock * 32, 0, st>>>(
-          static_cast<const T*>(y), ldy, H, asg_row, T_tokens, k, static_cast<const T*>(w),
-          static_cast<T*>(out), ldo);
-      return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
-    }
-  }
-  combine_kernel<T, false><<<grid, kRowsPerBlock * 32, 0, st>>>(
-        static_cast<const T*>(y), ldy, H, asg_row, T_tokens, k, static_cast<const T*>(w),
-        static_cast<T*>(out), ldo);
-  return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+  const T* yp = static_cast<const T*>(y);
+  const T* wp = static_cast<const T*>(w);
+  T* op = static_cast<T*>(out);
+  // source-row arrays sized to top_k (registers bound the resident blocks)
+  const int grid_v = grid_for(T_tokens * (H / 8), kThreadsPerBlock);
+  const int grid_s = grid_for(T_tokens * H, kThreadsPerBlock);
+#define MOE_COMBINE(KM)                                                                       \
+  do {                                                                                         \
+    if constexpr (sizeof(T) == 2) {                                                            \
+      if (vec)                                                                                 \
+        return launch_pdl(combine_kernel<T, true, KM>, grid_v, st, yp, ldy, H, asg_row,        \
+                          T_tokens, k, wp, op, ldo);                                           \
+    }                                                                                          \
+    return launch_pdl(combine_kernel<T, false, KM>, grid_s, st, yp, ldy, H, asg_row, T_tokens, \
+                      k, wp, op, ldo);                                                         \
+  } while (0)
+  if (k <= 1) MOE_COMBINE(1);
+  if (k <= 2) MOE_COMBINE(2);
+  if (k <= 4) MOE_COMBINE(4);
+  MOE_COMBINE(8);
+#undef MOE_COMBINE
 }
+
 
 }  // namespace
 

@@ -12,6 +12,7 @@
 //             rounding, bins / padded_bins / offsets, padding-row markers
 //   scatter : per unit, warp-synchronous stable ranks (match_any), writes the
 //             sorted order and both row maps
+// Problems of at most 8192 assignments run all three phases in one CTA.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -59,6 +60,8 @@ __device__ __forceinline__ int load_expert(const S* sel, long long i, int E, int
 template <typename S>
 __global__ void route_count_kernel(const S* __restrict__ sel, long long A, int E, long long U,
                                    long long units, int32_t* __restrict__ ws, int* status) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int hist[kWarpsPerBlock][kMaxE];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long unit = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + w;
@@ -113,6 +116,8 @@ __device__ int block_excl_scan(int v, int* total) {
 // unit's first assignment to expert e among all assignments to e.
 __global__ void route_scan_kernel(long long units, int E, int bs, int mode, int32_t* ws,
                                   RouteOut o) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int s_n[kMaxE], s_kept[kMaxE], s_pstart[kMaxE], s_padpre[kMaxE + 1];
   const int tid = threadIdx.x;
   // per-expert exclusive scan over units: 4 threads per expert column
@@ -189,6 +194,8 @@ template <typename S>
 __global__ void route_scatter_kernel(const S* __restrict__ sel, long long A, int E, long long U,
                                      long long units, const int32_t* __restrict__ ws,
                                      RouteOut o) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int base[kWarpsPerBlock][kMaxE];
   __shared__ int s_bstart[kMaxE], s_pstart[kMaxE], s_kept[kMaxE];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -235,6 +242,123 @@ __global__ void route_scatter_kernel(const S* __restrict__ sel, long long A, int
   }
 }
 
+// ---- single-CTA path for small problems ------------------------------------------
+// All three phases in one CTA of 32 warps (one launch instead of three): warp w
+// owns the contiguous chunk [w*U, (w+1)*U) of assignments; its per-expert
+// histogram row in shared memory becomes its running rank base.
+constexpr int kSmallWarps = 32;
+constexpr long long kSmallMaxA = 8192;
+
+template <typename S>
+__global__ void __launch_bounds__(kSmallWarps * 32, 1)
+    route_small_kernel(const S* __restrict__ sel, long long A, int E, int bs, int mode,
+                       RouteOut o) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ int hist[kSmallWarps][kMaxE];
+  __shared__ int s_kept[kMaxE], s_pstart[kMaxE], s_bstart[kMaxE], s_padpre[kMaxE + 1];
+  extern __shared__ int16_t s_sel[];  // [A] expert id of every assignment (-1: invalid)
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kSmallWarps * kMaxE; i += blockDim.x) (&hist[0][0])[i] = 0;
+  // one coalesced pass over the ids, eight independent loads in flight per thread
+  for (long long i0 = 0; i0 < A; i0 += 8LL * blockDim.x) {
+    S v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const long long i = i0 + j * blockDim.x + tid;
+      v[j] = i < A ? sel[i] : S(0);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const long long i = i0 + j * blockDim.x + tid;
+      if (i < A) {
+        const long long e = static_cast<long long>(v[j]);
+        const bool ok = e >= 0 && e < E;
+        if (!ok && o.status) atomicExch(o.status, kStatusBadExpert);
+        s_sel[i] = ok ? static_cast<int16_t>(e) : static_cast<int16_t>(-1);
+      }
+    }
+  }
+  __syncthreads();
+  const long long U = ((A + kSmallWarps - 1) / kSmallWarps + 31) / 32 * 32;
+  const long long beg = w * U, end = min(A, beg + U);
+  for (long long i = beg + lane; i < end; i += 32) {
+    const int e = s_sel[i];
+    if (e >= 0) atomicAdd(&hist[w][e], 1);
+  }
+  __syncthreads();
+  int n = 0;
+  if (tid < E) {
+    for (int ww = 0; ww < kSmallWarps; ++ww) {
+      const int c = hist[ww][tid];
+      hist[ww][tid] = n;
+      n += c;
+    }
+  }
+  int r = 0, kept = 0, pads = 0;
+  if (tid < E) {
+    r = rounded_count(n, bs, mode);
+    kept = min(n, r);
+    pads = r - kept;
+  }
+  int tot_kept, tot_round, tot_pad;
+  const int kept_ex = block_excl_scan(kept, &tot_kept);
+  const int round_ex = block_excl_scan(r, &tot_round);
+  const int pad_ex = block_excl_scan(pads, &tot_pad);
+  if (tid < E) {
+    s_kept[tid] = kept;
+    s_pstart[tid] = round_ex;
+    s_bstart[tid] = kept_ex;
+    s_padpre[tid] = pad_ex;
+    o.tpe[tid] = n;
+    o.bins[tid] = kept_ex + kept;
+    o.padded_bins[tid] = round_ex + r;
+    o.tok_off[tid] = round_ex;
+    o.ptpe[tid] = r;
+    if (tid == E - 1) o.tok_off[E] = round_ex + r;
+  }
+  __syncthreads();
+  const bool write_rows = o.row_asg != nullptr && static_cast<long long>(tot_round) <= o.p_cap;
+  if (o.row_asg != nullptr && !write_rows && tid == 0 && o.status)
+    atomicExch(o.status, kStatusCapacity);
+  if (write_rows) {
+    for (int p = tid; p < tot_pad; p += blockDim.x) {
+      int lo = 0, hi = E - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_padpre[mid] <= p) lo = mid;
+        else hi = mid - 1;
+      }
+      o.row_asg[s_pstart[lo] + s_kept[lo] + (p - s_padpre[lo])] = -1;
+    }
+  }
+  for (long long i0 = beg; i0 < end; i0 += 32) {
+    const long long i = i0 + lane;
+    const bool valid = i < end;
+    const int e = valid ? static_cast<int>(s_sel[i]) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0) {
+      const int rank = hist[w][e] + rank_in;
+      if (rank < s_kept[e]) {
+        const int pos = s_bstart[e] + rank;
+        o.bin_ids[pos] = e;
+        o.indices[pos] = static_cast<int32_t>(i);
+        const int row = s_pstart[e] + rank;
+        if (write_rows) o.row_asg[row] = static_cast<int32_t>(i);
+        if (o.asg_row) o.asg_row[i] = row;
+      } else if (o.asg_row) {
+        o.asg_row[i] = -1;
+      }
+    } else if (valid && o.asg_row) {
+      o.asg_row[i] = -1;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == 31 - __clz(peers)) hist[w][e] += __popc(peers);
+    __syncwarp();
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 long long unit_size(long long A) {
   // at most 256 units; at least 256 assignments (8 warp-steps) per unit
   long long U = (A + 255) / 256;
@@ -250,19 +374,51 @@ long long route_workspace_bytes(long long A, int E) {
   return (units > 0 ? units : 1) * E * 4;
 }
 
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kern, int grid, int block, int smem, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
 template <typename S>
 static int route_impl(const S* sel, long long A, int E, int bs, int mode, const RouteOut& o,
                       void* ws, long long ws_bytes, cudaStream_t st) {
+  if (A <= kSmallMaxA) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+      if (cudaFuncSetAttribute(route_small_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmallMaxA * 2)) != cudaSuccess)
+        return kStatusCuda;
+      attr_set[dev] = true;
+    }
+    const int rc = launch_pdl(route_small_kernel<S>, 1, kSmallWarps * 32,
+                              static_cast<int>(A * 2), st, sel, A, E, bs, mode, o);
+    if (rc != kStatusOk) return rc;
+    return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+  }
   const long long U = unit_size(A);
   const long long units = (A + U - 1) / U;
   if (ws_bytes < route_workspace_bytes(A, E)) return kStatusBadArg;
   int32_t* w = static_cast<int32_t*>(ws);
   const int blocks = static_cast<int>((units + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  if (units > 0)
-    route_count_kernel<S><<<blocks, kWarpsPerBlock * 32, 0, st>>>(sel, A, E, U, units, w, o.status);
-  route_scan_kernel<<<1, 1024, 0, st>>>(units, E, bs, mode, w, o);
-  if (units > 0)
-    route_scatter_kernel<S><<<blocks, kWarpsPerBlock * 32, 0, st>>>(sel, A, E, U, units, w, o);
+  int rc = launch_pdl(route_count_kernel<S>, blocks, kWarpsPerBlock * 32, 0, st, sel, A, E, U, units,
+                      w, o.status);
+  if (rc == kStatusOk) rc = launch_pdl(route_scan_kernel, 1, 1024, 0, st, units, E, bs, mode, w, o);
+  if (rc == kStatusOk)
+    rc = launch_pdl(route_scatter_kernel<S>, blocks, kWarpsPerBlock * 32, 0, st, sel, A, E, U, units,
+                    static_cast<const int32_t*>(w), o);
+  if (rc != kStatusOk) return rc;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }
 

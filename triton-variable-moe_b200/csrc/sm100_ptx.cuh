@@ -182,6 +182,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn_major, i
          | (static_cast<uint32_t>(M >> 4) << 24);         // M / 16
 }
 
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible / allow the next grid to launch.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ bool elect_one_lane() { return (threadIdx.x & 31) == 0; }
 
 }  // namespace moe

@@ -42,6 +42,7 @@ _SIGS = {
     "moe_route_workspace_bytes": [_L, _I],
     "moe_route": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _P, _P],
     "moe_route_no_alloc": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P],
+    "moe_router_topk": [_P, _L, _I, _I, _I, _P, _I, _P, _P],
     "moe_build_row_map": [_P, _P, _P, _P, _L, _L, _P, _L, _P, _P, _P],
     "moe_gather_map": [_P, _L, _I, _P, _P],
     "moe_padded_gather": [_P, _L, _L, _P, _I, _L, _P, _P, _P, _L, _I, _P],

@@ -146,8 +146,25 @@ def route(
     )
     _ev_end(ev, "route")
     check(rc, "moe_route")
-    _count(1 if A <= 65536 else 3)  # one fused CTA for small problems
+    _count(1 if A <= 8192 else 3)  # one fused CTA for small problems
     return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
+
+
+def router_topk(router_probs: torch.Tensor, top_k: int, normalize: bool, weights_dtype: torch.dtype):
+    """(weights [T, k] in weights_dtype, selected [T, k] int32) from fp32 router
+    probabilities: torch.topk order, lower index on ties, optional renorm."""
+    require_cuda(router_probs)
+    p = router_probs.float().contiguous()
+    T, E = p.shape
+    w = torch.empty(T, top_k, dtype=weights_dtype, device=p.device)
+    sel = torch.empty(T, top_k, dtype=torch.int32, device=p.device)
+    ev = _ev_begin()
+    rc = lib.moe_router_topk(ptr(p), T, E, int(top_k), 1 if normalize else 0, ptr(w),
+                             DTYPE_CODE[weights_dtype], ptr(sel), stream_handle(p.device))
+    _ev_end(ev, "router_topk")
+    check(rc, "moe_router_topk")
+    _count(1)
+    return w, sel
 
 
 def build_row_map(

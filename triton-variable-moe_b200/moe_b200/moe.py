@@ -229,10 +229,11 @@ class TritonMoEMLP(nn.Module):
     def _route_weights(self, x_flat):
         router_logits = self.router(x_flat)
         router_probs = F.sigmoid(router_logits.float())
-        top_k_weights, selected_experts = torch.topk(router_probs, self.num_active_experts, dim=-1)
-        if self.norm_topk_prob:
-            top_k_weights = top_k_weights / (top_k_weights.sum(dim=-1, keepdim=True) + 1e-20)
-        top_k_weights = top_k_weights.to(x_flat.dtype)
+        # top-k + renorm + cast in one kernel (moe.py:170-179); the weights get
+        # no gradient from the layer output in the reference either
+        # (scatter.py:160-176), so the choice is taken outside autograd
+        top_k_weights, selected_experts = _ops.router_topk(
+            router_probs.detach(), self.num_active_experts, self.norm_topk_prob, x_flat.dtype)
         return router_logits, router_probs, top_k_weights, selected_experts
 
     def _aux_losses(self, router_logits, router_probs, tokens_per_expert, dtype):
@@ -289,6 +290,7 @@ class TritonMoEMLP(nn.Module):
         batch_size, seq_len, n_embd = x.shape
         x_flat = x.reshape(batch_size * seq_len, n_embd)
         router_logits, router_probs, top_k_weights, selected_experts = self._route_weights(x_flat)
+        selected_experts = selected_experts.long()  # torch.topk's index dtype
         top_k_weights_flat = top_k_weights.reshape(-1)
         selected_experts_flat = selected_experts.reshape(-1)
         bin_ids, indices, tokens_per_expert, bins, padded_bins = fused_route(
