@@ -418,7 +418,7 @@ def run_b200(args, cfg, name):
 
     # per-kernel device time (CUDA events around each of our launches, eager steps)
     with torch.no_grad():
-        _, _, _, sel = layer._route_weights(x.detach().reshape(-1, H))
+        _, _, _, sel, _, _ = layer._route_weights(x.detach().reshape(-1, H))
         tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts).cpu().tolist()
     flops = gemm_flops(tpe, cfg)
     reps = 5

@@ -123,6 +123,31 @@ MOE_API int moe_router_topk(const float* router_probs, int64_t num_tokens, int n
                             int32_t* selected_experts, void* stream);
 
 /*
+ * Fused router head (triton_moe/moe.py:165-182 and the per-token part of the
+ * auxiliary losses, moe.py:253-268).  From router_logits [num_tokens,
+ * num_experts] (logits_dtype) in one pass:
+ *   router_probs [T, E] fp32 = sigmoid(logits);
+ *   selected_experts / weights as moe_router_topk;
+ *   lse [T] fp32 = logsumexp(logits_t) with torch's rounding chain in the
+ *   logits dtype; workspace (moe_router_head_workspace_floats floats):
+ *   per-block partial sums for the losses.
+ * moe_aux_losses then forms losses[0] = router_z_loss (mean lse^2, rounded to
+ * the logits dtype), losses[1] = load_balance_loss = sum_e lb_coef[e] * f_i[e]
+ * * p_i[e], losses[2] = compute_loss = mean_t sum_e probs * widths_normalized,
+ * f_i [E] = tokens_per_expert / sum (f_dtype) and p_i [E] fp32 = mean probs.
+ */
+MOE_API int64_t moe_router_head_workspace_floats(int64_t num_tokens, int num_experts);
+MOE_API int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tokens,
+                            int num_experts, int top_k, int normalize,
+                            const float* widths_normalized, float* router_probs, void* weights,
+                            int weights_dtype, int32_t* selected_experts, float* lse,
+                            float* workspace, void* stream);
+MOE_API int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,
+                           const int32_t* tokens_per_expert, const float* lb_coef,
+                           int logits_dtype, float* losses, void* f_i, int f_dtype, float* p_i,
+                           void* stream);
+
+/*
  * Padded-row maps from the reference's sorted-order metadata (indices,
  * bin_ids, bins, padded_bins as returned by fused_route).  The row arithmetic
  * is that of _padded_gather_kernel (triton_moe/kernels/gather.py:29-50).

@@ -118,6 +118,8 @@ def test_layer_is_deterministic(device):
 
 
 def test_aux_losses_match_reference_formulas(device):
+    """Fused router head + aux-loss kernels against the reference's fp32 golden
+    values (config c1v: variable widths, two size groups)."""
     d = LAYER["c1v"]
     H = int(d["n_embd"])
     sizes = [tuple(int(v) for v in s) for s in d["expert_sizes"]]
@@ -125,17 +127,46 @@ def test_aux_losses_match_reference_formulas(device):
     with torch.no_grad():
         m.router.weight.copy_(torch.from_numpy(d["router_w"]))
     x = torch.from_numpy(d["x"]).to(device)
-    inter = m.forward_with_intermediates  # routing only; aux losses are torch ops
-    logits, probs, _, _ = m._route_weights(x.reshape(-1, H))
+    logits, probs, w, sel, lse, ws = m._route_weights(x.reshape(-1, H))
+    np.testing.assert_array_equal(sel.reshape(-1).cpu().numpy(), d["selected"])
+    np.testing.assert_allclose(w.reshape(-1).cpu().numpy(), d["weights"], rtol=1e-6, atol=1e-7)
     from moe_b200.kernels import fused_route
 
     _, _, tpe, _, _ = fused_route(torch.from_numpy(d["selected"]).to(device), m.num_experts)
-    aux, f_i = m._aux_losses(logits, probs, tpe, torch.float32)
+    aux, f_i = m._aux_losses(logits, lse, ws, probs, tpe, torch.float32)
     np.testing.assert_allclose(f_i.cpu().numpy(), d["f_i"], rtol=1e-6)
     np.testing.assert_allclose(aux["router_z_loss"].item(), d["z_loss"], rtol=1e-5)
     np.testing.assert_allclose(aux["load_balance_loss"].item(), d["lb_loss"], rtol=1e-5)
     np.testing.assert_allclose(aux["compute_loss"].item(), d["compute_loss"], rtol=1e-5)
-    del inter
+
+
+@pytest.mark.parametrize("sizes,dtype", [([(4, 128)], torch.bfloat16), ([(2, 128), (3, 64), (1, 256)], torch.bfloat16),
+                                         ([(1, 128), (1, 64)], torch.float32), ([(4, 512), (8, 256), (4, 128)], torch.bfloat16)])
+def test_aux_losses_forward_and_gradients_match_torch(sizes, dtype, device):
+    """The fused aux losses and their gradients w.r.t. the router weight equal
+    the reference's torch expressions evaluated by autograd."""
+    H, k = 64, 2
+    E = sum(c for c, _ in sizes)
+    m = make_layer(H, sizes, min(k, E), 64, device=device, dtype=dtype)
+    x = torch.randn(300, H, device=device, dtype=dtype)
+    logits, probs, w, sel, lse, ws = m._route_weights(x)
+    from moe_b200.kernels import fused_route
+
+    _, _, tpe, _, _ = fused_route(sel.reshape(-1), E)
+    aux, f_i = m._aux_losses(logits, lse, ws, probs, tpe, dtype)
+    (aux["router_z_loss"].float() + aux["load_balance_loss"] + aux["compute_loss"]).backward()
+    g_fused = m.router.weight.grad.float().clone()
+    m.router.weight.grad = None
+    lg = m.router(x)
+    pr = torch.sigmoid(lg.float())
+    ref, f_ref = m._aux_losses_reference(lg, pr, tpe, dtype)
+    (ref["router_z_loss"].float() + ref["load_balance_loss"] + ref["compute_loss"]).backward()
+    g_ref = m.router.weight.grad.float()
+    assert torch.equal(f_i, f_ref)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    for key in aux:
+        torch.testing.assert_close(aux[key].float(), ref[key].float(), rtol=tol, atol=1e-6)
+    torch.testing.assert_close(g_fused, g_ref, rtol=5e-2, atol=1e-2 * g_ref.abs().max().item())
 
 
 def test_state_dict_layout_matches_reference(device):

@@ -22,6 +22,13 @@ int route_static_scratch(const void* sel, int sel_is_int64, long long A, int E, 
                          long long p_cap, int32_t* asg_row, int* status, cudaStream_t st);
 int router_topk(const float* probs, long long T, int E, int k, int norm, void* w, int w_dtype,
                 int32_t* sel, cudaStream_t st);
+int router_head_blocks(long long T);
+int router_head(const void* logits, int l_dtype, long long T, int E, int k, int norm,
+                const float* widths_norm, float* probs, void* w, int w_dtype, int32_t* sel,
+                float* lse, float* partials, int nblocks, cudaStream_t st);
+int aux_finalize(const float* partials, int nblocks, int E, long long T, const int32_t* tpe,
+                 const float* lb_coef, int l_dtype, float* losses, void* f_i, int f_dtype,
+                 float* p_i, cudaStream_t st);
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
                 long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
                 int dtype, cudaStream_t st);
@@ -127,6 +134,30 @@ int moe_router_topk(const float* router_probs, int64_t num_tokens, int num_exper
                     void* stream) {
   return moe::router_topk(router_probs, num_tokens, num_experts, top_k, normalize, weights,
                           weights_dtype, selected_experts, S(stream));
+}
+
+int64_t moe_router_head_workspace_floats(int64_t num_tokens, int num_experts) {
+  if (num_tokens < 0 || num_experts <= 0) return 0;
+  return static_cast<int64_t>(moe::router_head_blocks(num_tokens)) * (num_experts + 2);
+}
+
+int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tokens,
+                    int num_experts, int top_k, int normalize, const float* widths_normalized,
+                    float* router_probs, void* weights, int weights_dtype,
+                    int32_t* selected_experts, float* lse, float* workspace, void* stream) {
+  if (num_tokens == 0) return MOE_OK;
+  return moe::router_head(router_logits, logits_dtype, num_tokens, num_experts, top_k, normalize,
+                          widths_normalized, router_probs, weights, weights_dtype,
+                          selected_experts, lse, workspace, moe::router_head_blocks(num_tokens),
+                          S(stream));
+}
+
+int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,
+                   const int32_t* tokens_per_expert, const float* lb_coef, int logits_dtype,
+                   float* losses, void* f_i, int f_dtype, float* p_i, void* stream) {
+  return moe::aux_finalize(workspace, moe::router_head_blocks(num_tokens), num_experts,
+                           num_tokens, tokens_per_expert, lb_coef, logits_dtype, losses, f_i,
+                           f_dtype, p_i, S(stream));
 }
 
 int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,

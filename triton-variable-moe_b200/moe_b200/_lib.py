@@ -43,6 +43,9 @@ _SIGS = {
     "moe_route": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _P, _P],
     "moe_route_no_alloc": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P],
     "moe_router_topk": [_P, _L, _I, _I, _I, _P, _I, _P, _P],
+    "moe_router_head_workspace_floats": [_L, _I],
+    "moe_router_head": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P],
+    "moe_aux_losses": [_P, _L, _I, _P, _P, _I, _P, _P, _I, _P, _P],
     "moe_build_row_map": [_P, _P, _P, _P, _L, _L, _P, _L, _P, _P, _P],
     "moe_gather_map": [_P, _L, _I, _P, _P],
     "moe_padded_gather": [_P, _L, _L, _P, _I, _L, _P, _P, _P, _L, _I, _P],
@@ -61,6 +64,7 @@ _RESTYPE = {
     "moe_version": c_char_p,
     "moe_status_string": c_char_p,
     "moe_route_workspace_bytes": c_int64,
+    "moe_router_head_workspace_floats": c_int64,
 }
 
 EXPORTED = tuple(_SIGS)

@@ -167,6 +167,51 @@ def router_topk(router_probs: torch.Tensor, top_k: int, normalize: bool, weights
     return w, sel
 
 
+def router_head(router_logits: torch.Tensor, top_k: int, normalize: bool,
+                weights_dtype: torch.dtype, widths_normalized: torch.Tensor):
+    """One pass over the router logits: (probs fp32 [T,E], top-k weights [T,k],
+    selected int32 [T,k], per-token logsumexp fp32 [T], loss partials)."""
+    require_cuda(router_logits)
+    lg = router_logits.contiguous()
+    T, E = lg.shape
+    dev = lg.device
+    probs = torch.empty(T, E, dtype=torch.float32, device=dev)
+    w = torch.empty(T, top_k, dtype=weights_dtype, device=dev)
+    sel = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    lse = torch.empty(T, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(int(lib.moe_router_head_workspace_floats(T, E)), 1), dtype=torch.float32,
+                     device=dev)
+    wn = widths_normalized.float().contiguous()
+    ev = _ev_begin()
+    rc = lib.moe_router_head(ptr(lg), DTYPE_CODE[lg.dtype], T, E, int(top_k),
+                             1 if normalize else 0, ptr(wn), ptr(probs), ptr(w),
+                             DTYPE_CODE[weights_dtype], ptr(sel), ptr(lse), ptr(ws),
+                             stream_handle(dev))
+    _ev_end(ev, "router_head")
+    check(rc, "moe_router_head")
+    _count(1)
+    return probs, w, sel, lse, ws
+
+
+def aux_losses(ws: torch.Tensor, num_tokens: int, tokens_per_expert: torch.Tensor,
+               lb_coef: torch.Tensor, logits_dtype: torch.dtype, f_dtype: torch.dtype):
+    """(losses fp32 [3] = z, load balance, compute; f_i [E]; p_i fp32 [E])."""
+    dev = ws.device
+    E = tokens_per_expert.numel()
+    losses = torch.empty(3, dtype=torch.float32, device=dev)
+    f_i = torch.empty(E, dtype=f_dtype, device=dev)
+    p_i = torch.empty(E, dtype=torch.float32, device=dev)
+    ev = _ev_begin()
+    rc = lib.moe_aux_losses(ptr(ws), int(num_tokens), E, ptr(_meta(tokens_per_expert)),
+                            ptr(lb_coef.float().contiguous()), DTYPE_CODE[logits_dtype],
+                            ptr(losses), ptr(f_i), DTYPE_CODE[f_dtype], ptr(p_i),
+                            stream_handle(dev))
+    _ev_end(ev, "aux_losses")
+    check(rc, "moe_aux_losses")
+    _count(1)
+    return losses, f_i, p_i
+
+
 def build_row_map(
     indices: torch.Tensor,
     bin_ids: torch.Tensor,

@@ -141,6 +141,67 @@ class _MoEMLPFunction(torch.autograd.Function):
         return gx, gw1, gw2, None, None, None
 
 
+class _RouterHead(torch.autograd.Function):
+    """sigmoid + top-k + renorm + per-token logsumexp of the router logits in one
+    kernel.  Differentiable output: the fp32 probabilities (d sigmoid = p(1-p))."""
+
+    @staticmethod
+    def forward(ctx, logits, top_k, normalize, weights_dtype, widths_normalized):
+        probs, w, sel, lse, ws = _ops.router_head(logits, top_k, normalize, weights_dtype,
+                                                  widths_normalized)
+        ctx.save_for_backward(probs)
+        ctx.logits_dtype = logits.dtype
+        ctx.mark_non_differentiable(w, sel, lse, ws)
+        return probs, w, sel, lse, ws
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g_probs, _w, _sel, _lse, _ws):
+        (probs,) = ctx.saved_tensors
+        g = None
+        if g_probs is not None:
+            g = (g_probs * probs * (1.0 - probs)).to(ctx.logits_dtype)
+        return g, None, None, None, None
+
+
+class _AuxLosses(torch.autograd.Function):
+    """router_z_loss, load_balance_loss, compute_loss and f_i from the partial
+    sums of the router head (one kernel).  Backward restates the gradients of
+    the reference's torch expressions (moe.py:253-303)."""
+
+    @staticmethod
+    def forward(ctx, logits, probs, lse, ws, tokens_per_expert, lb_coef, widths_normalized,
+                f_dtype):
+        T = logits.shape[0]
+        losses, f_i, _p_i = _ops.aux_losses(ws, T, tokens_per_expert, lb_coef, logits.dtype,
+                                            f_dtype)
+        z = losses[0].to(logits.dtype)
+        lb = losses[1]
+        cl = losses[2]
+        ctx.save_for_backward(logits, lse, f_i, lb_coef, widths_normalized)
+        ctx.mark_non_differentiable(f_i)
+        return z, lb, cl, f_i
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g_z, g_lb, g_cl, _g_f):
+        logits, lse, f_i, lb_coef, wn = ctx.saved_tensors
+        T, E = logits.shape
+        g_logits = g_probs = None
+        if g_z is not None:
+            # d/dlogits mean_t lse_t^2 = (2 lse_t / T) softmax(logits_t)
+            coef = g_z.float() * 2.0 * lse / T
+            g_logits = (torch.softmax(logits.float(), dim=-1) * coef[:, None]).to(logits.dtype)
+        if g_lb is not None or g_cl is not None:
+            gp = torch.zeros(E, dtype=torch.float32, device=logits.device)
+            if g_cl is not None:
+                gp = gp + g_cl.float() * wn.float()
+            if g_lb is not None:
+                gp = gp + g_lb.float() * lb_coef.float() * f_i.float()
+            g_probs = (gp / T).expand(T, E)
+        return g_logits, g_probs, None, None, None, None, None, None
+
+
 class TritonMoEMLP(nn.Module):
     """Mixture-of-experts MLP with variable-width experts (drop-in for
     triton_moe.TritonMoEMLP)."""
@@ -212,6 +273,18 @@ class TritonMoEMLP(nn.Module):
             self.register_buffer("group_sizes", torch.tensor([1.0]), persistent=False)
             self.register_buffer("valid_expert_indices", torch.empty(0, dtype=torch.long),
                                  persistent=False)
+        # load_balance_loss = sum_e lb_coef[e] * f_i[e] * p_i[e]: the three cases of
+        # moe.py:276-303 (uniform widths, no size group with >1 expert, groups)
+        if len(set(self.expert_widths)) == 1:
+            coef = [float(self.num_experts)] * self.num_experts
+        elif self._num_valid_groups == 0:
+            coef = [1.0] * self.num_experts
+        else:
+            coef = [
+                (group_sizes[g] / self._num_valid_groups) if g >= 0 else 0.0
+                for g in expert_to_group
+            ]
+        self.register_buffer("_lb_coef", torch.tensor(coef, dtype=torch.float32), persistent=False)
         self._plan_cache: _Plan | None = None
 
     # ------------------------------------------------------------------ helpers
@@ -227,16 +300,22 @@ class TritonMoEMLP(nn.Module):
         return p
 
     def _route_weights(self, x_flat):
+        """(logits, probs, top-k weights, selected int32, lse, loss partials)."""
         router_logits = self.router(x_flat)
-        router_probs = F.sigmoid(router_logits.float())
-        # top-k + renorm + cast in one kernel (moe.py:170-179); the weights get
-        # no gradient from the layer output in the reference either
-        # (scatter.py:160-176), so the choice is taken outside autograd
-        top_k_weights, selected_experts = _ops.router_topk(
-            router_probs.detach(), self.num_active_experts, self.norm_topk_prob, x_flat.dtype)
-        return router_logits, router_probs, top_k_weights, selected_experts
+        router_probs, top_k_weights, selected, lse, ws = _RouterHead.apply(
+            router_logits, self.num_active_experts, self.norm_topk_prob, x_flat.dtype,
+            self.expert_widths_normalized)
+        return router_logits, router_probs, top_k_weights, selected, lse, ws
 
-    def _aux_losses(self, router_logits, router_probs, tokens_per_expert, dtype):
+    def _aux_losses(self, router_logits, lse, ws, router_probs, tokens_per_expert, dtype):
+        z, lb, cl, f_i = _AuxLosses.apply(router_logits, router_probs, lse, ws, tokens_per_expert,
+                                          self._lb_coef, self.expert_widths_normalized, dtype)
+        aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
+        return aux, f_i
+
+    def _aux_losses_reference(self, router_logits, router_probs, tokens_per_expert, dtype):
+        """The reference's torch expressions of the auxiliary losses (moe.py:253-272);
+        used as the checker of the fused kernels."""
         router_z_loss = torch.logsumexp(router_logits, dim=-1).pow(2).mean()
         f_i = (tokens_per_expert.float() / tokens_per_expert.sum()).to(dtype)
         load_balance_loss = self._compute_load_balance_loss(router_probs, f_i)
@@ -254,13 +333,14 @@ class TritonMoEMLP(nn.Module):
         """x: [batch, seq, n_embd] -> (output, aux_loss dict, f_i)."""
         batch_size, seq_len, n_embd = x.shape
         x_flat = x.reshape(batch_size * seq_len, n_embd)
-        router_logits, router_probs, top_k_weights, selected = self._route_weights(x_flat)
+        router_logits, router_probs, top_k_weights, selected, lse, ws = self._route_weights(x_flat)
         out_flat, tokens_per_expert = _MoEMLPFunction.apply(
             x_flat.to(self.w1.dtype), self.w1, self.w2, top_k_weights.reshape(-1),
             selected.reshape(-1), self._plan(),
         )
         output = out_flat.reshape(batch_size, seq_len, -1)
-        aux, f_i = self._aux_losses(router_logits, router_probs, tokens_per_expert, x.dtype)
+        aux, f_i = self._aux_losses(router_logits, lse, ws, router_probs, tokens_per_expert,
+                                    x.dtype)
         return output, aux, f_i
 
     def _compute_load_balance_loss(self, router_probs: torch.Tensor, f_i: torch.Tensor) -> torch.Tensor:
@@ -289,7 +369,8 @@ class TritonMoEMLP(nn.Module):
         """Forward returning every intermediate in the reference layout (moe.py:305-409)."""
         batch_size, seq_len, n_embd = x.shape
         x_flat = x.reshape(batch_size * seq_len, n_embd)
-        router_logits, router_probs, top_k_weights, selected_experts = self._route_weights(x_flat)
+        router_logits, router_probs, top_k_weights, selected_experts, _, _ = self._route_weights(
+            x_flat)
         selected_experts = selected_experts.long()  # torch.topk's index dtype
         top_k_weights_flat = top_k_weights.reshape(-1)
         selected_experts_flat = selected_experts.reshape(-1)
@@ -335,7 +416,8 @@ class TritonMoEMLP(nn.Module):
         with profiler.step("flatten"):
             x_flat = x.reshape(batch_size * seq_len, n_embd)
         with profiler.step("routing"):
-            router_logits, router_probs, top_k_weights, selected_experts = self._route_weights(x_flat)
+            router_logits, router_probs, top_k_weights, selected_experts, lse, ws = (
+                self._route_weights(x_flat))
             top_k_weights_flat = top_k_weights.reshape(-1)
             selected_experts_flat = selected_experts.reshape(-1)
         with profiler.step("fused_route"):
@@ -361,5 +443,6 @@ class TritonMoEMLP(nn.Module):
         with profiler.step("reshape"):
             output = output_flat.reshape(batch_size, seq_len, -1)
         with profiler.step("aux_loss"):
-            aux, f_i = self._aux_losses(router_logits, router_probs, tokens_per_expert, x.dtype)
+            aux, f_i = self._aux_losses(router_logits, lse, ws, router_probs, tokens_per_expert,
+                                        x.dtype)
         return output, aux, f_i
