@@ -18,8 +18,10 @@ Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
 events on the launch stream, with a 256 MiB write between steps to flush the
 126 MB L2; barrier + synchronize on both sides; the per-rank time is the sum
 of the K step times and the job time is the max over ranks.  `value` =
-tokens processed by all ranks / job time.  At N > 1 each rank runs its own
-replica of the workload (no collective on the data path): scaling "weak".
+tokens processed by all ranks / job time.  At N > 1 the layer is expert
+parallel: every rank keeps the workload's token batch (weak scaling) and the
+experts are sharded over the ranks, with NCCL all-to-all dispatch and combine;
+that step runs eagerly because the exchange sizes are read on the host.
 
 Extra keys: `roofline` (the grouped-GEMM engine: algorithmic FLOPs
 12*H*sum_e n_e*w_e per step / summed device time of its 6 launches per step,
@@ -262,6 +264,25 @@ def time_cpu_oracle(cfg, budget_s=15.0, tokens=None):
     return tokens / dt, tokens, reps
 
 
+def build_ep_layer(cfg, device, seed=0):
+    """The same layer (same seed, same full weights) with its experts sharded over
+    the ranks of the default process group."""
+    import torch
+
+    from moe_b200 import TritonMoEConfig
+    from moe_b200.ep import ExpertParallelMoEMLP
+
+    torch.manual_seed(seed)
+    mcfg = TritonMoEConfig(n_embd=cfg["n_embd"], expert_sizes=cfg["expert_sizes"],
+                           num_active_experts=cfg["top_k"], block_size=64)
+    full = build_layer(cfg, "cpu", seed)
+    layer = ExpertParallelMoEMLP(mcfg)
+    if cfg["zipf"]:
+        layer.router = full.router
+    layer.load_full_state_dict({k: v.float() for k, v in full.state_dict().items()})
+    return layer.to(device=device, dtype=torch.bfloat16)
+
+
 def capture_step(layer, x, gout):
     """Capture one fwd+bwd of the layer in a CUDA graph (the layer never
     synchronises the host, so the whole step is capturable).  Returns the graph,
@@ -345,11 +366,12 @@ def run_b200(args, cfg, name):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", device_id=dev)
 
     T = cfg["batch"] * cfg["seq"]
     H = cfg["n_embd"]
-    layer = build_layer(cfg, dev, seed=0)
+    layer = build_layer(cfg, dev, seed=0) if ws == 1 else build_ep_layer(cfg, dev, seed=0)
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
     x_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
     g_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
@@ -373,18 +395,28 @@ def run_b200(args, cfg, name):
         torch.cuda.synchronize()
         return 0
 
-    graph, out_static, per_step_launches = capture_step(layer, x, gout)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
+    if ws == 1:
+        graph, out_static, per_step_launches = capture_step(layer, x, gout)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        run_step = graph.replay
+    else:
+        # expert parallel: the exchange sizes are read on the host once per step,
+        # so the step runs eagerly (not captured)
+        l0 = _ops.launch_count
+        step(x, gout)
+        torch.cuda.synchronize()
+        per_step_launches = _ops.launch_count - l0
+        run_step = lambda: step(x, gout)  # noqa: E731
 
     # clock samples: a ~1.5 s soak of the same step right before the timed loop
     sampler = ClockSampler(gpu_selector(dev))
     sampler.start()
     t_end = time.perf_counter() + 1.5
     while time.perf_counter() < t_end:
-        for _ in range(20):
-            graph.replay()
+        for _ in range(20 if ws == 1 else 2):
+            run_step()
         torch.cuda.synchronize()
 
     def timed(fn, n):
@@ -409,7 +441,7 @@ def run_b200(args, cfg, name):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    job_ms = timed(graph.replay, args.steps)
+    job_ms = timed(run_step, args.steps)
     clocks = sampler.stop()
     launches = per_step_launches * args.steps
     ms_per_step = job_ms / args.steps
@@ -418,8 +450,16 @@ def run_b200(args, cfg, name):
 
     # per-kernel device time (CUDA events around each of our launches, eager steps)
     with torch.no_grad():
-        _, _, _, sel, _, _ = layer._route_weights(x.detach().reshape(-1, H))
-        tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts).cpu().tolist()
+        xf = x.detach().reshape(-1, H)
+        lg = layer.router(xf)
+        sel = torch.topk(torch.sigmoid(lg.float()), cfg["top_k"], dim=-1).indices
+        tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts)
+        if ws > 1:  # GEMM FLOPs of this rank: rows it receives for its own experts
+            dist.all_reduce(tpe)
+            mine = torch.zeros_like(tpe)
+            mine[layer.local_experts] = 1
+            tpe = tpe * mine
+        tpe = tpe.cpu().tolist()
     flops = gemm_flops(tpe, cfg)
     reps = 5
     per_kind: dict[str, float] = {}
@@ -469,8 +509,12 @@ def run_b200(args, cfg, name):
         with torch.no_grad():
             x.copy_(x_host, non_blocking=True)
             gout.copy_(g_host, non_blocking=True)
-        graph.replay()
-        out_host.copy_(out_static.detach(), non_blocking=True)
+        if ws == 1:
+            graph.replay()
+            out_host.copy_(out_static.detach(), non_blocking=True)
+        else:
+            out = step(x, gout)
+            out_host.copy_(out.detach(), non_blocking=True)
 
     e2e_ms = timed(e2e_step, args.steps)
     e2e_value = T * ws * args.steps / (e2e_ms / 1e3)
@@ -501,15 +545,18 @@ def run_b200(args, cfg, name):
                 "workload": workload_name(name, cfg),
                 "global_batch": cfg["batch"] * ws,
                 "seq_len": cfg["seq"],
-                "parallelism": f"{ws} independent replica(s)" if ws > 1 else "single GPU",
+                "parallelism": (f"expert parallel over {ws} GPUs ({layer.num_experts} experts "
+                                f"sharded, NCCL all-to-all dispatch/combine), {T} tokens per GPU")
+                if ws > 1 else "single GPU",
                 "l2": "flushed by a 256 MiB write between timed steps",
             },
             "roofline": roofline,
             "permute_roofline": permute,
             "kernel_us_per_step_eager": kernel_us,
             "eager_ms_per_step": eager_ms,
-            "execution": "step captured once in a CUDA graph and replayed (eager time in "
-                         "eager_ms_per_step)",
+            "execution": ("step captured once in a CUDA graph and replayed (eager time in "
+                          "eager_ms_per_step)") if ws == 1 else
+                         "eager (expert-parallel exchange sizes are read on the host)",
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
                     "d2h_bytes_per_step": nbytes},

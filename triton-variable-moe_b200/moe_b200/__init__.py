@@ -13,7 +13,15 @@ import sys
 from . import kernels
 from .moe import TritonMoEConfig, TritonMoEMLP
 
-__all__ = ["TritonMoEConfig", "TritonMoEMLP", "install_as_triton_moe"]
+__all__ = ["TritonMoEConfig", "TritonMoEMLP", "ExpertParallelMoEMLP", "install_as_triton_moe"]
+
+
+def __getattr__(name):
+    if name == "ExpertParallelMoEMLP":  # needs torch.distributed; imported on demand
+        from .ep import ExpertParallelMoEMLP
+
+        return ExpertParallelMoEMLP
+    raise AttributeError(name)
 
 
 def install_as_triton_moe() -> None:
