@@ -262,6 +262,27 @@ MOE_API int moe_grouped_gemm_down_dw(const void* inter, int64_t rows, int64_t ld
                              const int32_t* expert_weight_offsets, int num_experts,
                              void* grad_w2, int dtype, int tile_n, int* status, void* stream);
 
+/* The whole of grouped_gemm_down_backward (grouped_gemm.py:1293-1390) in one
+ * persistent launch: dIntermediate (or, with pre_act, the fused relu^2
+ * derivative) and dW2 share one tile list.  tile_n_width / tile_n_hidden are
+ * the N tiles of the two problems. */
+MOE_API int moe_grouped_gemm_down_backward(
+    const void* grad_y, int64_t rows, int64_t ld_grad_y, const void* inter, int64_t ld_inter,
+    const void* w2, int64_t hidden, int64_t total_width, const int32_t* expert_token_offsets,
+    const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert, int num_experts,
+    const void* pre_act, int64_t ld_pre, void* grad_inter, int64_t ld_grad_inter, void* grad_w2,
+    int dtype, int tile_n_width, int tile_n_hidden, int* status, void* stream);
+
+/* The GEMMs of grouped_gemm_up_backward (grouped_gemm.py:1165-1290) in one
+ * persistent launch: dX and dW1 from the activation gradient grad_act (the
+ * relu^2 derivative already applied). */
+MOE_API int moe_grouped_gemm_up_backward(
+    const void* grad_act, int64_t rows, int64_t ld_grad_act, const void* x, int64_t ld_x,
+    const void* w1, int64_t hidden, int64_t total_width, const int32_t* expert_token_offsets,
+    const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert, int num_experts,
+    void* grad_x, int64_t ld_grad_x, void* grad_w1, int dtype, int tile_n_width,
+    int tile_n_hidden, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -213,3 +213,40 @@ def test_fp16_up(device):
         r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]
         ref = t["x"][r0:r1].float() @ t["w1"][:, c0:c1].float()
         assert_close(out[r0:r1, : c1 - c0], ref, f"fp16 e{e}")
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_fused_backward_launches(case, device):
+    """The two-problem launches (dIntermediate+dW2, dX+dW1) give the same
+    results as the single-problem launches."""
+    from moe_b200.kernels import _ops
+
+    widths, counts, H, bs = case
+    t, m = make_problem(widths, counts, H, bs, device=device, seed=8)
+    args = (m["tok_off"], m["w_off"], m["tpe"], m["E"])
+    dact = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
+    gw2 = torch.full((m["TW"], H), 7.0, dtype=torch.bfloat16, device=device)
+    _ops.gemm_down_backward(t["gy"], t["ga"], t["w2"], *args, dact, gw2, pre_act=t["pre"],
+                            tile_n_width=128, tile_n_hidden=256)
+    dact_ref = torch.zeros_like(dact)
+    _ops.gemm_down_dinter(t["gy"], t["w2"], *args, dact_ref, pre_act=t["pre"])
+    gw2_ref = torch.zeros_like(gw2)
+    _ops.gemm_down_dw(t["ga"], t["gy"], m["tok_off"], m["w_off"], m["E"], gw2_ref, tile_n=256)
+    torch.cuda.synchronize()
+    assert torch.equal(dact, dact_ref)
+    assert torch.equal(gw2, gw2_ref)
+    gx = torch.zeros(m["rows"], H, dtype=torch.bfloat16, device=device)
+    gw1 = torch.full((H, m["TW"]), 7.0, dtype=torch.bfloat16, device=device)
+    _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1, tile_n_width=128,
+                          tile_n_hidden=256)
+    gx_ref = torch.zeros_like(gx)
+    _ops.gemm_up_dx(t["ga"], t["w1"], *args, gx_ref, tile_n=256)
+    gw1_ref = torch.zeros_like(gw1)
+    _ops.gemm_up_dw(t["x"], t["ga"], m["tok_off"], m["w_off"], m["E"], gw1_ref, tile_n=128)
+    torch.cuda.synchronize()
+    assert torch.equal(gx, gx_ref)
+    assert torch.equal(gw1, gw1_ref)
+    for e in range(m["E"]):
+        r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]
+        ref = t["x"][r0:r1].float().T @ t["ga"][r0:r1, : c1 - c0].float()
+        assert_close(gw1[:, c0:c1], ref, f"gw1 e{e}")

@@ -203,42 +203,203 @@ int moe_relu_squared_grad(const void* grad_out, const void* pre_act, int64_t row
   return moe::relu2_grad(grad_out, pre_act, rows, cols, ld, grad_act, dtype, S(stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+struct Built {
+  GemmOperands op;
+  GroupedGemmDesc g;
+  int epi;
+  int err;
+};
+
+Built bad(int err) {
+  Built b{};
+  b.err = err;
+  return b;
+}
+
+Built build_up(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_t hidden,
+               int64_t total_width, const int32_t* tok_off, const int32_t* w_off,
+               const int32_t* tpe, int E, int activation, void* out, void* pre_act,
+               int64_t ld_out, int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !x || !w1 || !out ||
+      ld_x < hidden || ld_out < 16 || ld_out % 8 != 0)
+    return bad(MOE_ERR_BAD_ARG);
+  if (activation != MOE_ACT_NONE && activation != MOE_ACT_RELU_SQUARED)
+    return bad(MOE_ERR_UNSUPPORTED);
+  Built b{};
+  b.g = base_desc(tok_off, tpe, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_TOKENS;
+  b.g.n_src = moe::DIM_WIDTH;
+  b.g.k_src = moe::DIM_CONST;
+  b.g.a_m_base = moe::BASE_TOK;
+  b.g.b_n_base = moe::BASE_WOFF;
+  b.g.d_m_base = moe::BASE_TOK;
+  b.g.d = out;
+  b.g.ldd = ld_out;
+  b.epi = moe::EPI_STORE;
+  if (activation == MOE_ACT_RELU_SQUARED) {
+    b.epi = moe::EPI_RELU2;
+    // without a pre_act buffer the relu output is written to `out` first and
+    // then overwritten by its square (same element, same thread)
+    b.g.aux = pre_act ? pre_act : out;
+    b.g.ld_aux = ld_out;
+  }
+  b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
+                      pick_bn(tile_n, 0), 0};
+  return b;
+}
+
+Built build_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
+                 int64_t hidden, int64_t total_width, const int32_t* tok_off,
+                 const int32_t* w_off, const int32_t* tpe, int E, void* out, int64_t ld_out,
+                 int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !inter || !w2 || !out ||
+      ld_inter < 16 || ld_inter % 8 != 0 || ld_out < hidden)
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, tpe, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_TOKENS;
+  b.g.n_src = moe::DIM_CONST;
+  b.g.k_src = moe::DIM_WIDTH;
+  b.g.a_m_base = moe::BASE_TOK;
+  b.g.b_k_base = moe::BASE_WOFF;
+  b.g.d_m_base = moe::BASE_TOK;
+  b.g.d = out;
+  b.g.ldd = ld_out;
+  b.epi = moe::EPI_STORE;
+  b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
+                      pick_bn(tile_n, hidden), 0};
+  return b;
+}
+
+Built build_up_dx(const void* grad_act, int64_t rows, int64_t ld_ga, const void* w1,
+                  int64_t hidden, int64_t total_width, const int32_t* tok_off,
+                  const int32_t* w_off, const int32_t* tpe, int E, void* grad_x, int64_t ld_gx,
+                  int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !grad_act || !w1 || !grad_x ||
+      ld_ga < 16 || ld_ga % 8 != 0 || ld_gx < hidden)
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, tpe, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_TOKENS;
+  b.g.n_src = moe::DIM_CONST;
+  b.g.k_src = moe::DIM_WIDTH;
+  b.g.a_m_base = moe::BASE_TOK;
+  b.g.b_k_base = moe::BASE_WOFF;
+  b.g.d_m_base = moe::BASE_TOK;
+  b.g.d = grad_x;
+  b.g.ldd = ld_gx;
+  b.epi = moe::EPI_STORE;
+  // B = w1 read K-major: rows are the hidden (N) index, columns the width (K)
+  b.op = GemmOperands{grad_act, rows, ld_ga, ld_ga, 0, w1, hidden, total_width, total_width, 0,
+                      pick_bn(tile_n, hidden), 0};
+  return b;
+}
+
+Built build_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_act, int64_t ld_ga,
+                  int64_t hidden, int64_t total_width, const int32_t* tok_off,
+                  const int32_t* w_off, int E, void* grad_w1, int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !x || !grad_act || !grad_w1 ||
+      ld_x < hidden || ld_ga < 16 || ld_ga % 8 != 0)
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, nullptr, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_CONST;
+  b.g.n_src = moe::DIM_WIDTH;
+  b.g.k_src = moe::DIM_TOKENS;
+  b.g.a_k_base = moe::BASE_TOK;
+  b.g.b_k_base = moe::BASE_TOK;
+  b.g.d_n_base = moe::BASE_WOFF;
+  b.g.d = grad_w1;
+  b.g.ldd = total_width;
+  b.epi = moe::EPI_STORE;
+  b.op = GemmOperands{x, rows, hidden, ld_x, 1, grad_act, rows, ld_ga, ld_ga, 1,
+                      pick_bn(tile_n, 0), 0};
+  return b;
+}
+
+Built build_down_dinter(const void* grad_y, int64_t rows, int64_t ld_gy, const void* w2,
+                        int64_t hidden, int64_t total_width, const int32_t* tok_off,
+                        const int32_t* w_off, const int32_t* tpe, int E, const void* pre_act,
+                        int64_t ld_pre, void* out, int64_t ld_out, int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !grad_y || !w2 || !out ||
+      ld_gy < hidden || ld_out < 16 || ld_out % 8 != 0 ||
+      (pre_act && (ld_pre < 16 || ld_pre % 8 != 0)))
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, tpe, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_TOKENS;
+  b.g.n_src = moe::DIM_WIDTH;
+  b.g.k_src = moe::DIM_CONST;
+  b.g.a_m_base = moe::BASE_TOK;
+  b.g.b_n_base = moe::BASE_WOFF;
+  b.g.d_m_base = moe::BASE_TOK;
+  b.g.d = out;
+  b.g.ldd = ld_out;
+  b.g.aux = const_cast<void*>(pre_act);
+  b.g.ld_aux = ld_pre;
+  b.epi = pre_act ? moe::EPI_DACT : moe::EPI_STORE;
+  // B = w2 read K-major: rows are the width (N) index, columns the hidden (K)
+  b.op = GemmOperands{grad_y, rows, hidden, ld_gy, 0, w2, total_width, hidden, hidden, 0,
+                      pick_bn(tile_n, 0), 0};
+  return b;
+}
+
+Built build_down_dw(const void* inter, int64_t rows, int64_t ld_inter, const void* grad_y,
+                    int64_t ld_gy, int64_t hidden, int64_t total_width, const int32_t* tok_off,
+                    const int32_t* w_off, int E, void* grad_w2, int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !inter || !grad_y ||
+      !grad_w2 || ld_inter < 16 || ld_inter % 8 != 0 || ld_gy < hidden)
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, nullptr, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_WIDTH;
+  b.g.n_src = moe::DIM_CONST;
+  b.g.k_src = moe::DIM_TOKENS;
+  b.g.a_k_base = moe::BASE_TOK;
+  b.g.b_k_base = moe::BASE_TOK;
+  b.g.d_m_base = moe::BASE_WOFF;
+  b.g.d = grad_w2;
+  b.g.ldd = hidden;
+  b.epi = moe::EPI_STORE;
+  b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_gy, 1,
+                      pick_bn(tile_n, hidden), 0};
+  return b;
+}
+
+int run1(const Built& b, int dtype, void* stream) {
+  if (b.err) return b.err;
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  return moe::run_grouped_gemm(b.op, b.g, b.epi, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+int run2(const Built& a, const Built& b, int dtype, void* stream) {
+  if (a.err) return a.err;
+  if (b.err) return b.err;
+  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
+  const GemmOperands ops[2] = {a.op, b.op};
+  const GroupedGemmDesc gs[2] = {a.g, b.g};
+  const int epis[2] = {a.epi, b.epi};
+  return moe::run_grouped_gemms(ops, gs, epis, 2, dtype == MOE_DTYPE_F16, S(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
 int moe_grouped_gemm_up(const void* x, int64_t rows, int64_t ld_x, const void* w1,
                         int64_t hidden, int64_t total_width,
                         const int32_t* expert_token_offsets,
                         const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert,
                         int num_experts, int activation, void* out, void* pre_act,
                         int64_t ld_out, int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !x || !w1 || !out || ld_x < hidden || ld_out < 16 || ld_out % 8 != 0)
-    return MOE_ERR_BAD_ARG;
-  if (activation != MOE_ACT_NONE && activation != MOE_ACT_RELU_SQUARED) return MOE_ERR_UNSUPPORTED;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_TOKENS;
-  g.n_src = moe::DIM_WIDTH;
-  g.k_src = moe::DIM_CONST;
-  g.a_m_base = moe::BASE_TOK;
-  g.a_k_base = moe::BASE_ZERO;
-  g.b_n_base = moe::BASE_WOFF;
-  g.b_k_base = moe::BASE_ZERO;
-  g.d_m_base = moe::BASE_TOK;
-  g.d_n_base = moe::BASE_ZERO;
-  g.d = out;
-  g.ldd = ld_out;
-  int epi = moe::EPI_STORE;
-  if (activation == MOE_ACT_RELU_SQUARED) {
-    epi = moe::EPI_RELU2;
-    // without a pre_act buffer the relu output is written to `out` first and
-    // then overwritten by its square (same element, same thread)
-    g.aux = pre_act ? pre_act : out;
-    g.ld_aux = ld_out;
-  }
-  GemmOperands op{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
-                  pick_bn(tile_n, 0), 0};
-  return moe::run_grouped_gemm(op, g, epi, dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_up(x, rows, ld_x, w1, hidden, total_width, expert_token_offsets,
+                       expert_weight_offsets, tokens_per_expert, num_experts, activation, out,
+                       pre_act, ld_out, tile_n, status),
+              dtype, stream);
 }
 
 int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
@@ -247,27 +408,10 @@ int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, con
                           const int32_t* expert_weight_offsets,
                           const int32_t* tokens_per_expert, int num_experts, void* out,
                           int64_t ld_out, int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !inter || !w2 || !out || ld_inter < 16 || ld_inter % 8 != 0 || ld_out < hidden)
-    return MOE_ERR_BAD_ARG;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_TOKENS;
-  g.n_src = moe::DIM_CONST;
-  g.k_src = moe::DIM_WIDTH;
-  g.a_m_base = moe::BASE_TOK;
-  g.a_k_base = moe::BASE_ZERO;
-  g.b_n_base = moe::BASE_ZERO;
-  g.b_k_base = moe::BASE_WOFF;
-  g.d_m_base = moe::BASE_TOK;
-  g.d_n_base = moe::BASE_ZERO;
-  g.d = out;
-  g.ldd = ld_out;
-  GemmOperands op{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
-                  pick_bn(tile_n, hidden), 0};
-  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_down(inter, rows, ld_inter, w2, hidden, total_width, expert_token_offsets,
+                         expert_weight_offsets, tokens_per_expert, num_experts, out, ld_out,
+                         tile_n, status),
+              dtype, stream);
 }
 
 int moe_grouped_gemm_up_dx(const void* grad_act, int64_t rows, int64_t ld_grad_act,
@@ -276,29 +420,10 @@ int moe_grouped_gemm_up_dx(const void* grad_act, int64_t rows, int64_t ld_grad_a
                            const int32_t* expert_weight_offsets,
                            const int32_t* tokens_per_expert, int num_experts, void* grad_x,
                            int64_t ld_grad_x, int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !grad_act || !w1 || !grad_x || ld_grad_act < 16 || ld_grad_act % 8 != 0 ||
-      ld_grad_x < hidden)
-    return MOE_ERR_BAD_ARG;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_TOKENS;
-  g.n_src = moe::DIM_CONST;
-  g.k_src = moe::DIM_WIDTH;
-  g.a_m_base = moe::BASE_TOK;
-  g.a_k_base = moe::BASE_ZERO;
-  g.b_n_base = moe::BASE_ZERO;
-  g.b_k_base = moe::BASE_WOFF;
-  g.d_m_base = moe::BASE_TOK;
-  g.d_n_base = moe::BASE_ZERO;
-  g.d = grad_x;
-  g.ldd = ld_grad_x;
-  // B = w1 read K-major: rows are the hidden (N) index, columns the width (K)
-  GemmOperands op{grad_act, rows, ld_grad_act, ld_grad_act, 0, w1, hidden, total_width,
-                  total_width, 0, pick_bn(tile_n, hidden), 0};
-  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_up_dx(grad_act, rows, ld_grad_act, w1, hidden, total_width,
+                          expert_token_offsets, expert_weight_offsets, tokens_per_expert,
+                          num_experts, grad_x, ld_grad_x, tile_n, status),
+              dtype, stream);
 }
 
 int moe_grouped_gemm_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_act,
@@ -306,27 +431,10 @@ int moe_grouped_gemm_up_dw(const void* x, int64_t rows, int64_t ld_x, const void
                            const int32_t* expert_token_offsets,
                            const int32_t* expert_weight_offsets, int num_experts,
                            void* grad_w1, int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !x || !grad_act || !grad_w1 || ld_x < hidden || ld_grad_act < 16 || ld_grad_act % 8 != 0)
-    return MOE_ERR_BAD_ARG;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, nullptr, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_CONST;
-  g.n_src = moe::DIM_WIDTH;
-  g.k_src = moe::DIM_TOKENS;
-  g.a_m_base = moe::BASE_ZERO;
-  g.a_k_base = moe::BASE_TOK;
-  g.b_n_base = moe::BASE_ZERO;
-  g.b_k_base = moe::BASE_TOK;
-  g.d_m_base = moe::BASE_ZERO;
-  g.d_n_base = moe::BASE_WOFF;
-  g.d = grad_w1;
-  g.ldd = total_width;
-  GemmOperands op{x, rows, hidden, ld_x, 1, grad_act, rows, ld_grad_act, ld_grad_act, 1,
-                  pick_bn(tile_n, 0), 0};
-  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_up_dw(x, rows, ld_x, grad_act, ld_grad_act, hidden, total_width,
+                          expert_token_offsets, expert_weight_offsets, num_experts, grad_w1,
+                          tile_n, status),
+              dtype, stream);
 }
 
 int moe_grouped_gemm_down_dinter(const void* grad_y, int64_t rows, int64_t ld_grad_y,
@@ -336,32 +444,10 @@ int moe_grouped_gemm_down_dinter(const void* grad_y, int64_t rows, int64_t ld_gr
                                  const int32_t* tokens_per_expert, int num_experts,
                                  const void* pre_act, int64_t ld_pre, void* out, int64_t ld_out,
                                  int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !grad_y || !w2 || !out || ld_grad_y < hidden || ld_out < 16 || ld_out % 8 != 0 ||
-      (pre_act && (ld_pre < 16 || ld_pre % 8 != 0)))
-    return MOE_ERR_BAD_ARG;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, tokens_per_expert, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_TOKENS;
-  g.n_src = moe::DIM_WIDTH;
-  g.k_src = moe::DIM_CONST;
-  g.a_m_base = moe::BASE_TOK;
-  g.a_k_base = moe::BASE_ZERO;
-  g.b_n_base = moe::BASE_WOFF;
-  g.b_k_base = moe::BASE_ZERO;
-  g.d_m_base = moe::BASE_TOK;
-  g.d_n_base = moe::BASE_ZERO;
-  g.d = out;
-  g.ldd = ld_out;
-  g.aux = const_cast<void*>(pre_act);
-  g.ld_aux = ld_pre;
-  // B = w2 read K-major: rows are the width (N) index, columns the hidden (K)
-  GemmOperands op{grad_y, rows, hidden, ld_grad_y, 0, w2, total_width, hidden, hidden, 0,
-                  pick_bn(tile_n, 0), 0};
-  return moe::run_grouped_gemm(op, g, pre_act ? moe::EPI_DACT : moe::EPI_STORE,
-                               dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_down_dinter(grad_y, rows, ld_grad_y, w2, hidden, total_width,
+                                expert_token_offsets, expert_weight_offsets, tokens_per_expert,
+                                num_experts, pre_act, ld_pre, out, ld_out, tile_n, status),
+              dtype, stream);
 }
 
 int moe_grouped_gemm_down_dw(const void* inter, int64_t rows, int64_t ld_inter,
@@ -369,27 +455,47 @@ int moe_grouped_gemm_down_dw(const void* inter, int64_t rows, int64_t ld_inter,
                              int64_t total_width, const int32_t* expert_token_offsets,
                              const int32_t* expert_weight_offsets, int num_experts,
                              void* grad_w2, int dtype, int tile_n, int* status, void* stream) {
-  if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  if (!common_ok(rows, hidden, total_width, expert_token_offsets, expert_weight_offsets,
-                 num_experts) ||
-      !inter || !grad_y || !grad_w2 || ld_inter < 16 || ld_inter % 8 != 0 || ld_grad_y < hidden)
-    return MOE_ERR_BAD_ARG;
-  GroupedGemmDesc g = base_desc(expert_token_offsets, nullptr, expert_weight_offsets,
-                                num_experts, hidden, status);
-  g.m_src = moe::DIM_WIDTH;
-  g.n_src = moe::DIM_CONST;
-  g.k_src = moe::DIM_TOKENS;
-  g.a_m_base = moe::BASE_ZERO;
-  g.a_k_base = moe::BASE_TOK;
-  g.b_n_base = moe::BASE_ZERO;
-  g.b_k_base = moe::BASE_TOK;
-  g.d_m_base = moe::BASE_WOFF;
-  g.d_n_base = moe::BASE_ZERO;
-  g.d = grad_w2;
-  g.ldd = hidden;
-  GemmOperands op{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_grad_y, 1,
-                  pick_bn(tile_n, hidden), 0};
-  return moe::run_grouped_gemm(op, g, moe::EPI_STORE, dtype == MOE_DTYPE_F16, S(stream));
+  return run1(build_down_dw(inter, rows, ld_inter, grad_y, ld_grad_y, hidden, total_width,
+                            expert_token_offsets, expert_weight_offsets, num_experts, grad_w2,
+                            tile_n, status),
+              dtype, stream);
+}
+
+int moe_grouped_gemm_down_backward(const void* grad_y, int64_t rows, int64_t ld_grad_y,
+                                   const void* inter, int64_t ld_inter, const void* w2,
+                                   int64_t hidden, int64_t total_width,
+                                   const int32_t* expert_token_offsets,
+                                   const int32_t* expert_weight_offsets,
+                                   const int32_t* tokens_per_expert, int num_experts,
+                                   const void* pre_act, int64_t ld_pre, void* grad_inter,
+                                   int64_t ld_grad_inter, void* grad_w2, int dtype,
+                                   int tile_n_width, int tile_n_hidden, int* status,
+                                   void* stream) {
+  return run2(build_down_dinter(grad_y, rows, ld_grad_y, w2, hidden, total_width,
+                                expert_token_offsets, expert_weight_offsets, tokens_per_expert,
+                                num_experts, pre_act, ld_pre, grad_inter, ld_grad_inter,
+                                tile_n_width, status),
+              build_down_dw(inter, rows, ld_inter, grad_y, ld_grad_y, hidden, total_width,
+                            expert_token_offsets, expert_weight_offsets, num_experts, grad_w2,
+                            tile_n_hidden, status),
+              dtype, stream);
+}
+
+int moe_grouped_gemm_up_backward(const void* grad_act, int64_t rows, int64_t ld_grad_act,
+                                 const void* x, int64_t ld_x, const void* w1, int64_t hidden,
+                                 int64_t total_width, const int32_t* expert_token_offsets,
+                                 const int32_t* expert_weight_offsets,
+                                 const int32_t* tokens_per_expert, int num_experts,
+                                 void* grad_x, int64_t ld_grad_x, void* grad_w1, int dtype,
+                                 int tile_n_width, int tile_n_hidden, int* status,
+                                 void* stream) {
+  return run2(build_up_dx(grad_act, rows, ld_grad_act, w1, hidden, total_width,
+                          expert_token_offsets, expert_weight_offsets, tokens_per_expert,
+                          num_experts, grad_x, ld_grad_x, tile_n_hidden, status),
+              build_up_dw(x, rows, ld_x, grad_act, ld_grad_act, hidden, total_width,
+                          expert_token_offsets, expert_weight_offsets, num_experts, grad_w1,
+                          tile_n_width, status),
+              dtype, stream);
 }
 
 }  // extern "C"

@@ -1,8 +1,13 @@
-// Persistent tcgen05 grouped GEMM: kernel template and host launcher.
+// Persistent tcgen05 grouped GEMM: kernel and host launcher.
+//
 // The six reference GEMM kernels (triton_moe/kernels/grouped_gemm.py:212-368,
-// 480-583, 654-802, 805-967, 970-1063, 1066-1162) are all instances of this
+// 480-583, 654-802, 805-967, 970-1063, 1066-1162) are all problems of this
 // one engine; they differ only in operand major-ness, in which metadata array
-// supplies each problem dimension, and in the epilogue.
+// supplies each problem dimension, in the N tile and in the epilogue -- all
+// runtime properties of a problem.  One launch runs up to kMaxProblems
+// independent problems over a single tile list (the backward's dIntermediate
+// + dW2 pair and dX + dW1 pair), so the SMs stay busy across the boundary
+// between them and a launch boundary disappears.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -10,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -21,29 +27,45 @@ namespace moe {
 
 namespace {
 
-constexpr int BM = 128;   // UMMA M: one TMEM lane per output row
-constexpr int BK = 64;    // k-block: one 128-byte swizzle row of bf16
-constexpr int UK = 16;    // K per tcgen05.mma (kind::f16)
+constexpr int BM = 128;  // UMMA M: one TMEM lane per output row
+constexpr int BK = 64;   // k-block: one 128-byte swizzle row of bf16
+constexpr int UK = 16;   // K per tcgen05.mma (kind::f16)
+constexpr int BN_MAX = 256;
 constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kABytes = BM * BK * 2;     // 16 KB
+constexpr int kRingBytes = 192 * 1024;   // smem ring for the A/B stages
+constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
+constexpr int kSmemBytes = 1024 + kRingBytes + kEpiBytes + 256;
 
-template <int BN>
-struct Cfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
-  static constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
-  static constexpr int kSmemBytes =
-      1024 /*align slack*/ + kStages * kStageBytes + kEpiBytes + 256 /*barriers*/;
+struct Problem {
+  GroupedGemmDesc g;
+  int a_mn, b_mn, epi, bn;
 };
 
-struct GroupTable {
-  int prefix[kMaxGroups + 1];
-  int M[kMaxGroups], N[kMaxGroups], K[kMaxGroups];
-  int am[kMaxGroups], ak[kMaxGroups], bn[kMaxGroups], bk[kMaxGroups];
-  int dm[kMaxGroups], dn[kMaxGroups];
+struct MultiParams {
+  CUtensorMap tmA[kMaxProblems];
+  CUtensorMap tmB[kMaxProblems];
+  Problem pr[kMaxProblems];
+  int nprob;
+  int stages;       // stages in the ring (depends on the largest N tile)
+  int stage_bytes;  // A tile + largest B tile
 };
+
+// Per (problem, expert) slot: tile prefix, extents and the two offsets every
+// coordinate base is made of (token offset, weight offset).
+struct Table {
+  int prefix[kMaxProblems * kMaxGroups + 1];
+  int M[kMaxProblems * kMaxGroups], N[kMaxProblems * kMaxGroups], K[kMaxProblems * kMaxGroups];
+  int tok[kMaxProblems * kMaxGroups], wof[kMaxProblems * kMaxGroups];
+};
+
+__device__ __forceinline__ int slot_base(int src, const Table& tb, int slot) {
+  if (src == BASE_TOK) return tb.tok[slot];
+  if (src == BASE_WOFF) return tb.wof[slot];
+  return 0;
+}
 
 __device__ __forceinline__ int dim_value(int src, int e, const GroupedGemmDesc& g) {
   if (src == DIM_TOKENS) return g.tok_off[e + 1] - g.tok_off[e];
@@ -91,48 +113,134 @@ struct Cvt<__half> {
   }
 };
 
-template <int BN>
-__device__ __forceinline__ void decode_tile(const GroupTable& tb, int E, int t, int& e,
-                                            int& m0, int& n0) {
-  int lo = 0, hi = E - 1;  // find e with prefix[e] <= t < prefix[e+1]
+struct Tile {
+  int p, e, m0, n0, slot;
+};
+
+__device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& P, int nge,
+                                            int t) {
+  int lo = 0, hi = nge - 1;  // last (problem, expert) slot with prefix <= t
   while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
+    const int mid = (lo + hi + 1) >> 1;
     if (tb.prefix[mid] <= t) lo = mid;
     else hi = mid - 1;
   }
-  e = lo;
-  const int local = t - tb.prefix[e];
-  const int ntn = (tb.N[e] + BN - 1) / BN;
-  m0 = (local / ntn) * BM;
-  n0 = (local % ntn) * BN;
+  Tile r;
+  r.p = lo < P.pr[0].g.E ? 0 : 1;  // slots are problem 0's experts, then problem 1's
+  r.e = lo - (r.p ? P.pr[0].g.E : 0);
+  r.slot = lo;
+  const int bn = P.pr[r.p].bn;
+  const int local = t - tb.prefix[lo];
+  const int ntn = (tb.N[lo] + bn - 1) / bn;
+  r.m0 = (local / ntn) * BM;
+  r.n0 = (local % ntn) * bn;
+  return r;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, typename T>
+// Compile-time operand configuration of a problem slot: bit 0 = A MN-major,
+// bit 1 = B MN-major, bit 2 = N tile 256 (else 128).
+constexpr int cfg_of(int a_mn, int b_mn, int bn) { return a_mn | (b_mn << 1) | ((bn == 256) << 2); }
+
+// Producer side of one tile: stream its k-blocks into the smem ring.
+template <int CFG>
+__device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint64_t* full,
+                                             uint64_t* empty, volatile int* abort_flag,
+                                             const void* tA, const void* tB, int nkb, int am,
+                                             int ak, int bn, int bk, int& stage,
+                                             uint32_t& phase) {
+  constexpr bool A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
+  constexpr int NT = (CFG & 4) ? 256 : 128;
+  constexpr uint32_t bytes = kABytes + NT * BK * 2;
+  for (int kb = 0; kb < nkb; ++kb) {
+    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
+    mbar_arrive_expect_tx(&full[stage], bytes);
+    uint8_t* a_dst = ring + stage * SB;
+    uint8_t* b_dst = a_dst + kABytes;
+    const int kc = kb * BK;
+    if constexpr (A_MN) {
+      tma_load_2d(a_dst, tA, &full[stage], am, ak + kc);
+      tma_load_2d(a_dst + 8192, tA, &full[stage], am + 64, ak + kc);
+    } else {
+      tma_load_2d(a_dst, tA, &full[stage], ak + kc, am);
+    }
+    if constexpr (B_MN) {
+#pragma unroll
+      for (int j = 0; j < NT / 64; ++j)
+        tma_load_2d(b_dst + j * 8192, tB, &full[stage], bn + 64 * j, bk + kc);
+    } else {
+      tma_load_2d(b_dst, tB, &full[stage], bk + kc, bn);
+    }
+    if (++stage == S) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+  return true;
+}
+
+// MMA side of one tile: issue its k-blocks into the TMEM accumulator.
+template <int CFG, int F16>
+__device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t* full,
+                                         uint64_t* empty, volatile int* abort_flag,
+                                         uint32_t d_tmem, int K, int nkb, int& stage,
+                                         uint32_t& phase) {
+  constexpr int A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
+  constexpr int NT = (CFG & 4) ? 256 : 128;
+  constexpr uint32_t idesc = idesc_f16(BM, NT, A_MN, B_MN, F16);
+  constexpr uint32_t a_step = A_MN ? 2048u : 32u, a_lbo = A_MN ? 8192u : 16u;
+  constexpr uint32_t b_step = B_MN ? 2048u : 32u, b_lbo = B_MN ? 8192u : 16u;
+  for (int kb = 0; kb < nkb; ++kb) {
+    if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
+    tc_fence_after();
+    const uint32_t a_addr = smem_u32(ring + stage * SB);
+    const uint32_t b_addr = a_addr + kABytes;
+    const int nk = min(BK, K - kb * BK) / UK;
+    if (nk == BK / UK) {
+#pragma unroll
+      for (int kk = 0; kk < BK / UK; ++kk)
+        tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + kk * a_step, a_lbo, 1024),
+                   smem_desc_sw128(b_addr + kk * b_step, b_lbo, 1024), idesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+    } else {
+      for (int kk = 0; kk < nk; ++kk)
+        tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + kk * a_step, a_lbo, 1024),
+                   smem_desc_sw128(b_addr + kk * b_step, b_lbo, 1024), idesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+    }
+    tc_commit(&empty[stage]);  // smem stage free once these MMAs retire
+    if (++stage == S) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+  return true;
+}
+
+template <typename T, int CFG0, int CFG1>
 __global__ void __launch_bounds__(kThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB,
-                        const GroupedGemmDesc g) {
-  using C = Cfg<BN>;
-  constexpr int S = C::kStages;
+    grouped_gemm_kernel(const __grid_constant__ MultiParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;                      // S stages of A
-  uint8_t* sB = smem + S * C::kABytes;     // S stages of B
-  uint8_t* sEpi = smem + S * C::kStageBytes;  // epilogue staging, 4 KB per warp
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + C::kEpiBytes);
+  const int S = P.stages;
+  const int SB = P.stage_bytes;
+  uint8_t* ring = smem;               // stage s: A at s*SB, B at s*SB + kABytes
+  uint8_t* sEpi = smem + kRingBytes;  // epilogue staging, 4 KB per warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
   uint64_t* full = bars;
-  uint64_t* empty = bars + S;
-  uint64_t* acc_full = bars + 2 * S;
-  uint64_t* acc_empty = bars + 2 * S + 2;
-  uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* acc_full = bars + 2 * kMaxStages;
+  uint64_t* acc_empty = bars + 2 * kMaxStages + 2;
+  uint64_t* drain = bars + 2 * kMaxStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 5);
 
-  __shared__ GroupTable tb;
+  __shared__ Table tb;
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // (problem, expert) slots: problem 0's experts, then problem 1's
+  const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -149,11 +257,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    for (int p = 0; p < P.nprob; ++p) {
+      tma_prefetch_desc(&P.tmA[p]);
+      tma_prefetch_desc(&P.tmB[p]);
+    }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
     tc_fence_before();
   }
@@ -162,48 +272,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   // produce or consume, so wait for them (programmatic dependent launch).
   griddep_wait();
   if (warp == 2) {
-    // Per-expert geometry and the tile prefix table: lane L owns a contiguous
-    // chunk of experts, then a warp scan turns chunk sums into offsets.
-    const int E = g.E;
-    const int per = (E + 31) / 32;
+    // Per-(problem, expert) geometry and the tile prefix table: lane L owns a
+    // contiguous chunk of slots, then a warp scan turns chunk sums into offsets.
+    const int per = (nge + 31) / 32;
     const int beg = lane * per;
-    const int end = min(E, beg + per);
+    const int end = min(nge, beg + per);
     int sum = 0;
-    for (int e = beg; e < end; ++e) {
-      int M = dim_value(g.m_src, e, g);
-      if (g.m_src == DIM_TOKENS && g.tok_cnt != nullptr) M = min(M, g.tok_cnt[e]);
-      M = max(M, 0);
-      const int N = dim_value(g.n_src, e, g);
-      const int K = dim_value(g.k_src, e, g);
-      tb.M[e] = M;
-      tb.N[e] = N;
-      tb.K[e] = max(K, 0);
-      tb.am[e] = base_value(g.a_m_base, e, g);
-      tb.ak[e] = base_value(g.a_k_base, e, g);
-      tb.bn[e] = base_value(g.b_n_base, e, g);
-      tb.bk[e] = base_value(g.b_k_base, e, g);
-      tb.dm[e] = base_value(g.d_m_base, e, g);
-      tb.dn[e] = base_value(g.d_n_base, e, g);
-      // TMA needs 16-byte aligned inner coordinates and the MMA consumes K in
-      // steps of 16: reject (and skip) any expert whose geometry breaks that.
-      const bool bad = (K % 16) != 0 || (g.n_src == DIM_WIDTH && N % 16 != 0) ||
-                       (g.m_src == DIM_WIDTH && M % 16 != 0) || (tb.bn[e] % 8) != 0 ||
-                       (tb.bk[e] % 8) != 0 || (tb.dn[e] % 8) != 0;
-      if (bad && g.status != nullptr) atomicExch(g.status, kStatusBadArg);
-      const int tiles =
-          (!bad && M > 0 && N > 0) ? ((M + BM - 1) / BM) * ((N + BN - 1) / BN) : 0;
-      tb.prefix[e] = sum;  // chunk-local exclusive prefix for now
+    for (int s = beg; s < end; ++s) {
+      const int p = s < P.pr[0].g.E ? 0 : 1;
+      const int e = s - (p ? P.pr[0].g.E : 0);
+      const GroupedGemmDesc& g = P.pr[p].g;
+      int M = 0, N = 0, K = 0, tiles = 0;
+      {
+        M = dim_value(g.m_src, e, g);
+        if (g.m_src == DIM_TOKENS && g.tok_cnt != nullptr) M = min(M, g.tok_cnt[e]);
+        M = max(M, 0);
+        N = dim_value(g.n_src, e, g);
+        K = max(dim_value(g.k_src, e, g), 0);
+        // TMA needs 16-byte aligned inner coordinates and the MMA consumes K in
+        // steps of 16: reject (and skip) any expert whose geometry breaks that.
+        const bool bad = (K % 16) != 0 || (g.n_src == DIM_WIDTH && N % 16 != 0) ||
+                         (g.m_src == DIM_WIDTH && M % 16 != 0) ||
+                         (base_value(g.b_n_base, e, g) % 8) != 0 ||
+                         (base_value(g.b_k_base, e, g) % 8) != 0 ||
+                         (base_value(g.d_n_base, e, g) % 8) != 0;
+        if (bad && g.status != nullptr) atomicExch(g.status, kStatusBadArg);
+        const int bn = P.pr[p].bn;
+        tiles = (!bad && M > 0 && N > 0) ? ((M + BM - 1) / BM) * ((N + bn - 1) / bn) : 0;
+      }
+      tb.M[s] = M;
+      tb.N[s] = N;
+      tb.K[s] = K;
+      tb.tok[s] = g.tok_off[e];
+      tb.wof[s] = g.w_off[e];
+      tb.prefix[s] = sum;  // chunk-local exclusive prefix for now
       sum += tiles;
     }
     int incl = sum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      int v = __shfl_up_sync(0xffffffffu, incl, o);
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
     const int excl = incl - sum;
-    for (int e = beg; e < end; ++e) tb.prefix[e] += excl;
-    if (lane == 31) tb.prefix[E] = incl;
+    for (int s = beg; s < end; ++s) tb.prefix[s] += excl;
+    if (lane == 31) tb.prefix[nge] = incl;
   }
   __syncthreads();
   tc_fence_after();
@@ -211,96 +324,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   // completion before touching memory.
   griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
-  const int E = g.E;
-  const int total = tb.prefix[E];
+  const int total = tb.prefix[nge];
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        int e, m0, n0;
-        decode_tile<BN>(tb, E, t, e, m0, n0);
-        const int K = tb.K[e];
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const Tile tl = decode_tile(tb, P, nge, t);
+        const Problem& pr = P.pr[tl.p];
+        const GroupedGemmDesc& g = pr.g;
+        const int K = tb.K[tl.slot];
         const int nkb = (K + BK - 1) / BK;
-        const int am = tb.am[e] + m0, ak = tb.ak[e];
-        const int bn = tb.bn[e] + n0, bk = tb.bk[e];
-        bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          uint8_t* a_dst = sA + stage * C::kABytes;
-          uint8_t* b_dst = sB + stage * C::kBBytes;
-          const int kc = kb * BK;
-          if constexpr (A_MN) {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], am + 64 * j, ak + kc);
-          } else {
-            tma_load_2d(a_dst, &tmA, &full[stage], ak + kc, am);
-          }
-          if constexpr (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], bn + 64 * j, bk + kc);
-          } else {
-            tma_load_2d(b_dst, &tmB, &full[stage], bk + kc, bn);
-          }
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
+        const int am = slot_base(g.a_m_base, tb, tl.slot) + tl.m0;
+        const int ak = slot_base(g.a_k_base, tb, tl.slot);
+        const int bn = slot_base(g.b_n_base, tb, tl.slot) + tl.n0;
+        const int bk = slot_base(g.b_k_base, tb, tl.slot);
+        if (tl.p == 0)
+          ok = produce_tile<CFG0>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0], &P.tmB[0],
+                                  nkb, am, ak, bn, bk, stage, phase);
+        else
+          ok = produce_tile<CFG1>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1], &P.tmB[1],
+                                  nkb, am, ak, bn, bk, stage, phase);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc =
-          idesc_f16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0, std::is_same<T, __half>::value ? 1 : 0);
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int e, m0, n0;
-        decode_tile<BN>(tb, E, t, e, m0, n0);
-        const int K = tb.K[e];
+        const Tile tl = decode_tile(tb, P, nge, t);
+        const int K = tb.K[tl.slot];
         const int nkb = (K + BK - 1) / BK;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * C::kABytes);
-          const uint32_t b_addr = smem_u32(sB + stage * C::kBBytes);
-          const int kvalid = min(BK, K - kb * BK);
-          const int nk = kvalid / UK;
-          for (int kk = 0; kk < nk; ++kk) {
-            uint64_t ad, bd;
-            if constexpr (A_MN) ad = smem_desc_sw128(a_addr + kk * 2048, 8192, 1024);
-            else ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-            if constexpr (B_MN) bd = smem_desc_sw128(b_addr + kk * 2048, 8192, 1024);
-            else bd = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            tc_mma_f16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&empty[stage]);  // smem stage free once these MMAs retire
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN_MAX);
+        constexpr int F16 = std::is_same<T, __half>::value ? 1 : 0;
+        if (tl.p == 0)
+          ok = mma_tile<CFG0, F16>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
+                                   phase);
+        else
+          ok = mma_tile<CFG1, F16>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
+                                   phase);
         if (!ok) break;
         if (nkb > 0) tc_commit(&acc_full[buf]);
         else mbar_arrive(&acc_full[buf]);
@@ -324,26 +396,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stg = sEpi + q * 4096;
     int buf = 0;
     uint32_t acc_phase = 0;
-    T* D = reinterpret_cast<T*>(g.d);
-    T* AUX = reinterpret_cast<T*>(g.aux);
     const int rsub = lane >> 3;  // row within a 4-row group for the row-major phase
     const int csub = lane & 7;   // 16-byte chunk within a 128-byte row
     auto stg_chunk = [&](int row, int chunk) -> uint4* {
       return reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4));
     };
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      int e, m0, n0;
-      decode_tile<BN>(tb, E, t, e, m0, n0);
-      const int M = tb.M[e], N = tb.N[e], K = tb.K[e];
+      const Tile tl = decode_tile(tb, P, nge, t);
+      const Problem& pr = P.pr[tl.p];
+      const GroupedGemmDesc& g = pr.g;
+      const int slot = tl.slot;
+      const int M = tb.M[slot], N = tb.N[slot], K = tb.K[slot];
+      const int epi = pr.epi;
+      T* D = reinterpret_cast<T*>(g.d);
+      T* AUX = reinterpret_cast<T*>(g.aux);
       if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag)) break;
       tc_fence_after();
-      const int rbase = m0 + q * 32;            // group row of this warp's first row
-      const int rows_ok = min(32, M - rbase);   // may be <= 0
-      const long long grow0 = static_cast<long long>(tb.dm[e]) + rbase;
-      const int gcol0 = tb.dn[e] + n0;
-      const int ncols = min(BN, N - n0);
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      const int rbase = tl.m0 + q * 32;        // group row of this warp's first row
+      const int rows_ok = min(32, M - rbase);  // may be <= 0
+      const long long grow0 = static_cast<long long>(slot_base(g.d_m_base, tb, slot)) + rbase;
+      const int gcol0 = slot_base(g.d_n_base, tb, slot) + tl.n0;
+      const int ncols = min(pr.bn, N - tl.n0);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(buf * BN_MAX);
       // row-major store of the staged slab (rows beyond the expert and columns
       // beyond its width are skipped); all shared loads first, then the stores
       auto store_slab = [&](T* dst, long long ld, int s, int cvalid) {
@@ -368,50 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 64; ++i) v[i] = 0.f;
         }
-        if constexpr (EPI == EPI_STORE) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 o;
-            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
-            *stg_chunk(lane, j) = o;
-          }
-          __syncwarp();
-          store_slab(D, g.ldd, s, cvalid);
-          __syncwarp();
-        } else if constexpr (EPI == EPI_RELU2) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 o;
-            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              v[j * 8 + 2 * i] = fmaxf(v[j * 8 + 2 * i], 0.f);
-              v[j * 8 + 2 * i + 1] = fmaxf(v[j * 8 + 2 * i + 1], 0.f);
-              op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
-            }
-            *stg_chunk(lane, j) = o;
-          }
-          __syncwarp();
-          store_slab(AUX, g.ld_aux, s, cvalid);
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 o;
-            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float a = v[j * 8 + 2 * i], b = v[j * 8 + 2 * i + 1];
-              op[i] = Cvt<T>::pack(a * a, b * b);
-            }
-            *stg_chunk(lane, j) = o;
-          }
-          __syncwarp();
-          store_slab(D, g.ldd, s, cvalid);
-          __syncwarp();
-        } else {  // EPI_DACT: stage pre (row-major, coalesced), combine per row
-          uint4 pv[8];  // all eight loads in flight before any shared store
+        if (epi == EPI_DACT) {
+          // stage pre (row-major, coalesced; all eight loads in flight first)
+          uint4 pv[8];
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int row = it * 4 + rsub;
@@ -442,6 +476,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           store_slab(D, g.ldd, s, cvalid);
           __syncwarp();
+        } else {
+          if (epi == EPI_RELU2) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] = fmaxf(v[i], 0.f);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 o;
+            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
+            *stg_chunk(lane, j) = o;
+          }
+          __syncwarp();
+          if (epi == EPI_RELU2) {
+            store_slab(AUX, g.ld_aux, s, cvalid);  // pre = relu(acc)
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint4 o;
+              uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float a = v[j * 8 + 2 * i], b = v[j * 8 + 2 * i + 1];
+                op[i] = Cvt<T>::pack(a * a, b * b);
+              }
+              *stg_chunk(lane, j) = o;
+            }
+            __syncwarp();
+          }
+          store_slab(D, g.ldd, s, cvalid);
+          __syncwarp();
         }
       }
       tc_fence_before();
@@ -455,9 +521,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (threadIdx.x == 0 && abort_flag && g.status != nullptr) atomicExch(g.status, kStatusTimeout);
+  if (threadIdx.x == 0 && abort_flag) {
+    for (int p = 0; p < P.nprob; ++p)
+      if (P.pr[p].g.status != nullptr) atomicExch(P.pr[p].g.status, kStatusTimeout);
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -493,16 +562,14 @@ int make_tmap(CUtensorMap* tm, const void* base, int is_f16, long long inner, lo
   return r == CUDA_SUCCESS ? kStatusOk : kStatusBadArg;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, typename T>
-int launch_inst(const CUtensorMap& ta, const CUtensorMap& tbm, const GroupedGemmDesc& g,
-                int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<BN, A_MN, B_MN, EPI, T>;
-  constexpr int smem = Cfg<BN>::kSmemBytes;
+template <typename T, int C0, int C1>
+int launch(const MultiParams& P, int grid, cudaStream_t st) {
+  auto kern = grouped_gemm_kernel<T, C0, C1>;
   static bool attr_set[64] = {};  // per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
             cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
             cudaSuccess)
@@ -517,28 +584,44 @@ int launch_inst(const CUtensorMap& ta, const CUtensorMap& tbm, const GroupedGemm
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tbm, g) != cudaSuccess) return kStatusCuda;
+  if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return kStatusCuda;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }
 
-template <int BN, int EPI, typename T>
-int dispatch_major(const GemmOperands& op, const CUtensorMap& ta, const CUtensorMap& tbm,
-                   const GroupedGemmDesc& g, int grid, cudaStream_t st) {
-  if (!op.a_mn && !op.b_mn) return launch_inst<BN, false, false, EPI, T>(ta, tbm, g, grid, st);
-  if (!op.a_mn && op.b_mn) return launch_inst<BN, false, true, EPI, T>(ta, tbm, g, grid, st);
-  if (op.a_mn && op.b_mn) return launch_inst<BN, true, true, EPI, T>(ta, tbm, g, grid, st);
-  return kStatusUnsupported;  // MN-major A with K-major B is not used by any MoE GEMM
+// One problem: any of the 8 operand configurations.
+template <typename T, int C>
+int launch_single_cfg(const MultiParams& P, int grid, cudaStream_t st) {
+  return launch<T, C, C>(P, grid, st);
 }
-
-template <int EPI, typename T>
-int dispatch_bn(const GemmOperands& op, int bn, const CUtensorMap& ta, const CUtensorMap& tbm,
-                const GroupedGemmDesc& g, int grid, cudaStream_t st) {
-  if (bn == 256) return dispatch_major<256, EPI, T>(op, ta, tbm, g, grid, st);
-  return dispatch_major<128, EPI, T>(op, ta, tbm, g, grid, st);
+template <typename T>
+int launch_single(int c, const MultiParams& P, int grid, cudaStream_t st) {
+  switch (c) {
+    case 0: return launch_single_cfg<T, 0>(P, grid, st);
+    case 1: return launch_single_cfg<T, 1>(P, grid, st);
+    case 2: return launch_single_cfg<T, 2>(P, grid, st);
+    case 3: return launch_single_cfg<T, 3>(P, grid, st);
+    case 4: return launch_single_cfg<T, 4>(P, grid, st);
+    case 5: return launch_single_cfg<T, 5>(P, grid, st);
+    case 6: return launch_single_cfg<T, 6>(P, grid, st);
+    default: return launch_single_cfg<T, 7>(P, grid, st);
+  }
+}
+// Two problems: a K-major/K-major problem followed by an MN-major/MN-major one
+// (the backward pairs), any N tiles.  Returns kStatusUnsupported otherwise.
+template <typename T>
+int launch_pair(int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
+  if ((c0 & 3) != 0 || (c1 & 3) != 3) return kStatusUnsupported;
+  const int k = ((c0 >> 2) & 1) | (((c1 >> 2) & 1) << 1);
+  switch (k) {
+    case 0: return launch<T, 0, 3>(P, grid, st);
+    case 1: return launch<T, 4, 3>(P, grid, st);
+    case 2: return launch<T, 0, 7>(P, grid, st);
+    default: return launch<T, 4, 7>(P, grid, st);
+  }
 }
 
 }  // namespace
@@ -554,32 +637,72 @@ int num_sms() {
   return n;
 }
 
+int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
+                      int is_f16, cudaStream_t st) {
+  if (n <= 0 || n > kMaxProblems) return kStatusBadArg;
+  MultiParams P;
+  memset(&P, 0, sizeof(P));
+  int bn_max = 128, grid = 0, used = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmOperands& op = ops[i];
+    const GroupedGemmDesc& g = gs[i];
+    if (g.E == 0) continue;
+    if (g.E < 0 || g.E > kMaxGroups) return kStatusUnsupported;
+    if (op.a_rows <= 0 || op.a_cols <= 0 || op.b_rows <= 0 || op.b_cols <= 0)
+      return kStatusBadArg;
+    const int bn = op.bn == 256 ? 256 : 128;
+    int s;
+    // A is [a_rows, a_cols] row-major.  K-major A: rows are M, columns are K.
+    // MN-major A: rows are K, columns are M.
+    if (op.a_mn) s = make_tmap(&P.tmA[used], op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, 64);
+    else s = make_tmap(&P.tmA[used], op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, BM);
+    if (s) return s;
+    if (op.b_mn) s = make_tmap(&P.tmB[used], op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, 64);
+    else s = make_tmap(&P.tmB[used], op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, bn);
+    if (s) return s;
+    P.pr[used].g = g;
+    P.pr[used].a_mn = op.a_mn;
+    P.pr[used].b_mn = op.b_mn;
+    P.pr[used].epi = epis[i];
+    P.pr[used].bn = bn;
+    bn_max = bn > bn_max ? bn : bn_max;
+    if (op.grid > grid) grid = op.grid;
+    ++used;
+  }
+  if (used == 0) return kStatusOk;
+  P.nprob = used;
+  P.stage_bytes = kABytes + bn_max * BK * 2;
+  P.stages = kRingBytes / P.stage_bytes;
+  if (P.stages > kMaxStages) P.stages = kMaxStages;
+  if (grid <= 0) grid = num_sms();
+  const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn);
+  if (used == 1)
+    return is_f16 ? launch_single<__half>(c0, P, grid, st)
+                  : launch_single<__nv_bfloat16>(c0, P, grid, st);
+  const int c1 = cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn);
+  int rc = is_f16 ? launch_pair<__half>(c0, c1, P, grid, st)
+                  : launch_pair<__nv_bfloat16>(c0, c1, P, grid, st);
+  if (rc != kStatusUnsupported) return rc;
+  // no compiled pair for these configurations: one launch per problem
+  for (int i = 0; i < used; ++i) {
+    MultiParams Q = P;
+    Q.nprob = 1;
+    Q.tmA[0] = P.tmA[i];
+    Q.tmB[0] = P.tmB[i];
+    Q.pr[0] = P.pr[i];
+    Q.stage_bytes = kABytes + P.pr[i].bn * BK * 2;
+    Q.stages = kRingBytes / Q.stage_bytes > kMaxStages ? kMaxStages : kRingBytes / Q.stage_bytes;
+    const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn);
+    rc = is_f16 ? launch_single<__half>(ci, Q, grid, st)
+                : launch_single<__nv_bfloat16>(ci, Q, grid, st);
+    if (rc != kStatusOk) return rc;
+  }
+  return kStatusOk;
+}
+
 int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int is_f16,
                      cudaStream_t st) {
-  if (g.E <= 0) return kStatusOk;
-  if (g.E > kMaxGroups) return kStatusUnsupported;
-  if (op.a_rows <= 0 || op.a_cols <= 0 || op.b_rows <= 0 || op.b_cols <= 0)
-    return kStatusBadArg;
-  const int bn = op.bn == 256 ? 256 : 128;
-  CUtensorMap ta, tbm;
-  int s;
-  // A is [a_rows, a_cols] row-major.  K-major A: rows are M, columns are K.
-  // MN-major A: rows are K, columns are M.
-  if (op.a_mn) s = make_tmap(&ta, op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, 64);
-  else s = make_tmap(&ta, op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, BM);
-  if (s) return s;
-  if (op.b_mn) s = make_tmap(&tbm, op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, 64);
-  else s = make_tmap(&tbm, op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, bn);
-  if (s) return s;
-  const int grid = op.grid > 0 ? op.grid : num_sms();
-  if (is_f16) {
-    if (epi == EPI_STORE) return dispatch_bn<EPI_STORE, __half>(op, bn, ta, tbm, g, grid, st);
-    if (epi == EPI_RELU2) return dispatch_bn<EPI_RELU2, __half>(op, bn, ta, tbm, g, grid, st);
-    return dispatch_bn<EPI_DACT, __half>(op, bn, ta, tbm, g, grid, st);
-  }
-  if (epi == EPI_STORE) return dispatch_bn<EPI_STORE, __nv_bfloat16>(op, bn, ta, tbm, g, grid, st);
-  if (epi == EPI_RELU2) return dispatch_bn<EPI_RELU2, __nv_bfloat16>(op, bn, ta, tbm, g, grid, st);
-  return dispatch_bn<EPI_DACT, __nv_bfloat16>(op, bn, ta, tbm, g, grid, st);
+  return run_grouped_gemms(&op, &g, &epi, 1, is_f16, st);
 }
 
 }  // namespace moe

@@ -37,6 +37,7 @@ enum EpiMode : int {
 };
 
 constexpr int kMaxGroups = 256;
+constexpr int kMaxProblems = 2;  // independent problems per launch
 
 struct GroupedGemmDesc {
   // expert metadata (device, int32)

@@ -17,7 +17,7 @@ constexpr int kStatusBadExpert = -6;
 
 struct GroupedGemmDesc;
 
-// Dense operand views for one grouped GEMM launch.  Both operands are
+// Dense operand views of one grouped GEMM problem.  Both operands are
 // row-major [rows, cols] with a row stride in elements.  `a_mn` / `b_mn`
 // select the MN-major reading (rows are the reduction dimension).
 struct GemmOperands {
@@ -33,6 +33,9 @@ struct GemmOperands {
 
 int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int is_f16,
                      cudaStream_t st);
+// Up to kMaxProblems independent grouped GEMMs in one persistent launch.
+int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
+                      int is_f16, cudaStream_t st);
 
 int num_sms();
 

@@ -58,6 +58,12 @@ _SIGS = {
     "moe_grouped_gemm_down_dinter": [
         _P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _P, _L, _I, _I, _P, _P,
     ],
+    "moe_grouped_gemm_down_backward": [
+        _P, _L, _L, _P, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _P, _L, _P, _I, _I, _I, _P, _P,
+    ],
+    "moe_grouped_gemm_up_backward": [
+        _P, _L, _L, _P, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _P, _I, _I, _I, _P, _P,
+    ],
     "moe_grouped_gemm_down_dw": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _I, _P, _I, _I, _P, _P],
 }
 _RESTYPE = {

@@ -177,16 +177,15 @@ class _EPMoEFunction(torch.autograd.Function):
         src = gyr if R > 0 else torch.zeros(1, H, device=dev, dtype=dt)
         _ops.gather(src, lr2a, 1, cap, out=gy, rows_device=p_dev)
         dact = torch.empty(rows, lp.max_width, device=dev, dtype=dt)
-        _ops.gemm_down_dinter(gy, w2, ltok, lp.w_off, None, e_loc, dact, pre_act=pre,
-                              tile_n=lp.tile_n_width)
         gw2 = torch.empty_like(w2)
-        _ops.gemm_down_dw(h, gy, ltok, lp.w_off, e_loc, gw2, tile_n=lp.tile_n_hidden)
+        _ops.gemm_down_backward(gy, h, w2, ltok, lp.w_off, None, e_loc, dact, gw2, pre_act=pre,
+                                tile_n_width=lp.tile_n_width, tile_n_hidden=lp.tile_n_hidden)
         gw1 = torch.empty_like(w1)
-        _ops.gemm_up_dw(xg, dact, ltok, lp.w_off, e_loc, gw1, tile_n=lp.tile_n_width)
+        gxg = torch.empty(rows, H, device=dev, dtype=dt) if ctx.needs_input_grad[0] else None
+        _ops.gemm_up_backward(dact, xg, w1, ltok, lp.w_off, None, e_loc, gxg, gw1,
+                              tile_n_width=lp.tile_n_width, tile_n_hidden=lp.tile_n_hidden)
         gx = None
-        if ctx.needs_input_grad[0]:
-            gxg = torch.empty(rows, H, device=dev, dtype=dt)
-            _ops.gemm_up_dx(dact, w1, ltok, lp.w_off, None, e_loc, gxg, tile_n=lp.tile_n_hidden)
+        if gxg is not None:
             gx_recv = _ops.combine(gxg, la2r, R, 1, weights=None)
             gxs = exchange_rows(gx_recv, ctx.recv, ctx.send, plan.group)
             gx = _ops.combine(gxs, a2r, T, k, weights=None)

@@ -435,3 +435,44 @@ def gemm_down_dw(inter, grad_y, tok_off, w_off, num_experts, out, tile_n=0):
     check(rc, "moe_grouped_gemm_down_dw")
     _count(1)
     return out
+
+
+def gemm_down_backward(grad_y, inter, w2, tok_off, w_off, tok_cnt, num_experts, grad_inter, grad_w2,
+                       pre_act=None, tile_n_width=0, tile_n_hidden=0):
+    """dIntermediate (relu^2 derivative fused when pre_act is given) and dW2 in one launch."""
+    _gemm_check(grad_y, inter, w2, grad_inter, grad_w2)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    TW, H = w2.shape
+    ld_pre = pre_act.stride(0) if pre_act is not None else 0
+    ev = _ev_begin()
+    rc = lib.moe_grouped_gemm_down_backward(
+        ptr(grad_y), grad_y.shape[0], grad_y.stride(0), ptr(inter), inter.stride(0), ptr(w2), H,
+        TW, ptr(tok_off), ptr(w_off), ptr(tok_cnt), int(num_experts), ptr(pre_act), ld_pre,
+        ptr(grad_inter), grad_inter.stride(0), ptr(grad_w2), DTYPE_CODE[grad_y.dtype],
+        int(tile_n_width), int(tile_n_hidden), ptr(status_buffer(w2.device)),
+        stream_handle(w2.device),
+    )
+    _ev_end(ev, "grouped_gemm_down_backward")
+    check(rc, "moe_grouped_gemm_down_backward")
+    _count(1)
+
+
+def gemm_up_backward(grad_act, x, w1, tok_off, w_off, tok_cnt, num_experts, grad_x, grad_w1,
+                     tile_n_width=0, tile_n_hidden=0):
+    """dX and dW1 from the activation gradient in one launch (grad_x may be None:
+    dW1 only)."""
+    if grad_x is None:
+        return gemm_up_dw(x, grad_act, tok_off, w_off, num_experts, grad_w1, tile_n=tile_n_width)
+    _gemm_check(grad_act, x, w1, grad_x, grad_w1)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    H, TW = w1.shape
+    ev = _ev_begin()
+    rc = lib.moe_grouped_gemm_up_backward(
+        ptr(grad_act), grad_act.shape[0], grad_act.stride(0), ptr(x), x.stride(0), ptr(w1), H, TW,
+        ptr(tok_off), ptr(w_off), ptr(tok_cnt), int(num_experts), ptr(grad_x), grad_x.stride(0),
+        ptr(grad_w1), DTYPE_CODE[grad_act.dtype], int(tile_n_width), int(tile_n_hidden),
+        ptr(status_buffer(w1.device)), stream_handle(w1.device),
+    )
+    _ev_end(ev, "grouped_gemm_up_backward")
+    check(rc, "moe_grouped_gemm_up_backward")
+    _count(1)

@@ -149,11 +149,9 @@ def grouped_gemm_up_backward(
     else:
         grad_act = g
     E = len(expert_widths)
-    w1c = w1.contiguous()
-    _ops.gemm_up_dx(grad_act, w1c, expert_token_offsets, expert_weight_offsets, tokens_per_expert,
-                    E, grad_x)
     xs = _gather_rows(x, gather_map, total_tokens) if gather_map is not None else x.contiguous()
-    _ops.gemm_up_dw(xs, grad_act, expert_token_offsets, expert_weight_offsets, E, grad_w1)
+    _ops.gemm_up_backward(grad_act, xs, w1.contiguous(), expert_token_offsets, expert_weight_offsets,
+                          tokens_per_expert, E, grad_x, grad_w1)
     return grad_x, grad_w1
 
 
@@ -178,11 +176,8 @@ def grouped_gemm_down_backward(
         return grad_inter, grad_w2
     g = grad_output.to(intermediate.dtype).contiguous()
     E = len(expert_widths)
-    w2c = w2.contiguous()
-    _ops.gemm_down_dinter(g, w2c, expert_token_offsets, expert_weight_offsets, tokens_per_expert,
-                          E, grad_inter)
-    _ops.gemm_down_dw(intermediate.contiguous(), g, expert_token_offsets, expert_weight_offsets,
-                      E, grad_w2)
+    _ops.gemm_down_backward(g, intermediate.contiguous(), w2.contiguous(), expert_token_offsets,
+                            expert_weight_offsets, tokens_per_expert, E, grad_inter, grad_w2)
     return grad_inter, grad_w2
 
 

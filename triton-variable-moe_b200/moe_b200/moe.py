@@ -119,25 +119,23 @@ class _MoEMLPFunction(torch.autograd.Function):
         # scatter backward: weighted gather of the output gradient
         gy = torch.empty(rows, H, device=dev, dtype=dt)
         _ops.gather(grad_out, r2a, k, cap, out=gy, rows_device=p_dev, weights=weights)
-        # down backward: dIntermediate with the relu^2 derivative fused, then dW2
+        # down backward: dIntermediate with the relu^2 derivative fused, and dW2,
+        # in one launch
         dact = torch.empty(rows, plan.max_width, device=dev, dtype=dt)
-        _ops.gemm_down_dinter(gy, w2, tok_off, plan.w_off, None, E, dact, pre_act=pre,
-                              tile_n=plan.tile_n_width)
-        gw2 = torch.empty_like(w2) if ctx.needs_input_grad[2] else None
-        if gw2 is not None:
-            _ops.gemm_down_dw(h, gy, tok_off, plan.w_off, E, gw2, tile_n=plan.tile_n_hidden)
-        # up backward: dX (gathered space) and dW1
-        gx = None
-        if ctx.needs_input_grad[0]:
-            gxg = torch.empty(rows, H, device=dev, dtype=dt)
-            _ops.gemm_up_dx(dact, w1, tok_off, plan.w_off, None, E, gxg,
-                            tile_n=plan.tile_n_hidden)
-            # gather backward: unit-weight combine of the k copies of each token
-            gx = _ops.combine(gxg, a2r, ctx.T, k, weights=None)
-        gw1 = None
-        if ctx.needs_input_grad[1]:
-            gw1 = torch.empty_like(w1)
-            _ops.gemm_up_dw(xg, dact, tok_off, plan.w_off, E, gw1, tile_n=plan.tile_n_width)
+        gw2 = torch.empty_like(w2)
+        _ops.gemm_down_backward(gy, h, w2, tok_off, plan.w_off, None, E, dact, gw2, pre_act=pre,
+                                tile_n_width=plan.tile_n_width, tile_n_hidden=plan.tile_n_hidden)
+        # up backward: dX (gathered space) and dW1 in one launch
+        gxg = torch.empty(rows, H, device=dev, dtype=dt) if ctx.needs_input_grad[0] else None
+        gw1 = torch.empty_like(w1)
+        _ops.gemm_up_backward(dact, xg, w1, tok_off, plan.w_off, None, E, gxg, gw1,
+                              tile_n_width=plan.tile_n_width, tile_n_hidden=plan.tile_n_hidden)
+        # gather backward: unit-weight combine of the k copies of each token
+        gx = _ops.combine(gxg, a2r, ctx.T, k, weights=None) if gxg is not None else None
+        if not ctx.needs_input_grad[1]:
+            gw1 = None
+        if not ctx.needs_input_grad[2]:
+            gw2 = None
         return gx, gw1, gw2, None, None, None
 
 
