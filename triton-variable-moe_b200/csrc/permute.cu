@@ -85,9 +85,12 @@ __device__ __forceinline__ void pdl_done() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+constexpr int kVecPerLane = 4;  // 16-byte vectors in flight per lane per batch
+
 // out[r, :] = src row map[r] / div of x (times w[map[r]] when w != null);
 // rows whose map entry is negative are zero.  Rows at or beyond *rows_dev
-// (when given) are not touched.  One thread per 8-element (16-byte) chunk.
+// (when given) are not touched.  One warp per row; each lane issues up to four
+// 16-byte loads before its stores, so a 1024-wide bf16 row is one round trip.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreadsPerBlock)
     gather_rows_kernel(const T* __restrict__ x, long long ldx, int H,
@@ -97,38 +100,45 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
   pdl_wait();
   long long nrows = rows;
   if (rows_dev != nullptr) nrows = min(nrows, static_cast<long long>(*rows_dev));
-  constexpr int V = VEC ? 8 : 1;
-  const int per_row = (H + V - 1) / V;
-  const long long n = nrows * per_row;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / per_row;
-    const int c = static_cast<int>(i - r * per_row) * V;
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < nrows; r += warps) {
     const int a = __ldg(map + r);
-    T* o = out + r * ldo + c;
+    T* orow = out + r * ldo;
     if constexpr (VEC) {
-      if (a < 0) {
-        *reinterpret_cast<uint4*>(o) = make_uint4(0, 0, 0, 0);
-      } else {
-        const uint4 u =
-            __ldg(reinterpret_cast<const uint4*>(x + static_cast<long long>(a / div) * ldx + c));
-        if (w == nullptr) {
-          *reinterpret_cast<uint4*>(o) = u;
-        } else {
-          float f[8];
-          V8<T>::load(u, f);
-          const float sc = V8<T>::to_f(w[a]);
+      const T* xrow = a >= 0 ? x + static_cast<long long>(a / div) * ldx : nullptr;
+      const float sc = (a >= 0 && w != nullptr) ? V8<T>::to_f(w[a]) : 1.f;
+      for (int c0 = 0; c0 < H; c0 += 32 * 8 * kVecPerLane) {
+        uint4 u[kVecPerLane];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) f[k] *= sc;
-          *reinterpret_cast<uint4*>(o) = V8<T>::store(f);
+        for (int j = 0; j < kVecPerLane; ++j) {
+          const int c = c0 + (j * 32 + lane) * 8;
+          u[j] = make_uint4(0, 0, 0, 0);
+          if (xrow != nullptr && c < H) u[j] = __ldg(reinterpret_cast<const uint4*>(xrow + c));
+        }
+#pragma unroll
+        for (int j = 0; j < kVecPerLane; ++j) {
+          const int c = c0 + (j * 32 + lane) * 8;
+          if (c >= H) break;
+          if (w != nullptr && xrow != nullptr) {
+            float f[8];
+            V8<T>::load(u[j], f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f[q] *= sc;
+            u[j] = V8<T>::store(f);
+          }
+          *reinterpret_cast<uint4*>(orow + c) = u[j];
         }
       }
     } else {
-      if (a < 0) {
-        *o = V8<T>::from_f(0.f);
-      } else {
-        const T v = x[static_cast<long long>(a / div) * ldx + c];
-        *o = w ? V8<T>::from_f(V8<T>::to_f(v) * V8<T>::to_f(w[a])) : v;
+      for (int c = lane; c < H; c += 32) {
+        if (a < 0) {
+          orow[c] = V8<T>::from_f(0.f);
+        } else {
+          const T v = x[static_cast<long long>(a / div) * ldx + c];
+          orow[c] = w ? V8<T>::from_f(V8<T>::to_f(v) * V8<T>::to_f(w[a])) : v;
+        }
       }
     }
   }
@@ -136,64 +146,80 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
 }
 
 // out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding).
-// One thread per 8-element chunk of a token; the k source rows are loaded
-// independently so their latencies overlap.
+// One warp per token; the k source rows' vectors are all loaded before any is
+// used.
 template <typename T, bool VEC, int kMaxK>
 __global__ void __launch_bounds__(kThreadsPerBlock)
     combine_kernel(const T* __restrict__ y, long long ldy, int H,
                    const int32_t* __restrict__ asg_row, long long T_tokens, int k,
                    const T* __restrict__ w, T* __restrict__ out, long long ldo) {
   pdl_wait();
-  constexpr int V = VEC ? 8 : 1;
-  const int per_row = (H + V - 1) / V;
-  const long long n = T_tokens * per_row;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long t = i / per_row;
-    const int c = static_cast<int>(i - t * per_row) * V;
-    float acc[V];
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  constexpr int NV = VEC ? (kMaxK <= 2 ? 4 : 2) : 1;  // vectors per lane per batch
+  for (long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       t < T_tokens; t += warps) {
+    T* orow = out + t * ldo;
+    if constexpr (VEC) {
+      for (int c0 = 0; c0 < H; c0 += 32 * 8 * NV) {
+        float acc[NV][8];
 #pragma unroll
-    for (int q = 0; q < V; ++q) acc[q] = 0.f;
-    for (int j0 = 0; j0 < k; j0 += kMaxK) {
-      const int kk = min(kMaxK, k - j0);
-      int rows[kMaxK];
-      float sc[kMaxK];
+        for (int v = 0; v < NV; ++v)
 #pragma unroll
-      for (int j = 0; j < kMaxK; ++j) {
-        rows[j] = j < kk ? __ldg(asg_row + t * k + j0 + j) : -1;
-        sc[j] = (j < kk && w != nullptr) ? V8<T>::to_f(w[t * k + j0 + j]) : 1.f;
-      }
-      if constexpr (VEC) {
-        uint4 u[kMaxK];
+          for (int q = 0; q < 8; ++q) acc[v][q] = 0.f;
+        for (int j0 = 0; j0 < k; j0 += kMaxK) {  // top-k beyond kMaxK: more batches
+          const int kk = min(kMaxK, k - j0);
+          int rows[kMaxK];
+          float sc[kMaxK];
+          uint4 u[kMaxK][NV];
 #pragma unroll
-        for (int j = 0; j < kMaxK; ++j)
-          if (rows[j] >= 0) u[j] = __ldg(reinterpret_cast<const uint4*>(y + rows[j] * ldy + c));
+          for (int j = 0; j < kMaxK; ++j) {
+            rows[j] = j < kk ? __ldg(asg_row + t * k + j0 + j) : -1;
+            sc[j] = (j < kk && w != nullptr) ? V8<T>::to_f(w[t * k + j0 + j]) : 1.f;
+          }
 #pragma unroll
-        for (int j = 0; j < kMaxK; ++j) {
-          if (rows[j] < 0) continue;
-          float f[8];
-          V8<T>::load(u[j], f);
-          if (w != nullptr) {
+          for (int j = 0; j < kMaxK; ++j)
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[q] += V8<T>::rnd(f[q] * sc[j]);
-          } else {
+            for (int v = 0; v < NV; ++v) {
+              const int c = c0 + (v * 32 + lane) * 8;
+              if (rows[j] >= 0 && c < H)
+                u[j][v] = __ldg(reinterpret_cast<const uint4*>(y + rows[j] * ldy + c));
+            }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[q] += f[q];
+          for (int j = 0; j < kMaxK; ++j) {
+            if (rows[j] < 0) continue;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+              if (c0 + (v * 32 + lane) * 8 >= H) continue;
+              float f[8];
+              V8<T>::load(u[j][v], f);
+              if (w != nullptr) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[v][q] += V8<T>::rnd(f[q] * sc[j]);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[v][q] += f[q];
+              }
+            }
           }
         }
-      } else {
 #pragma unroll
-        for (int j = 0; j < kMaxK; ++j) {
-          if (rows[j] < 0) continue;
-          const float v = V8<T>::to_f(y[rows[j] * ldy + c]);
-          acc[0] += (w != nullptr) ? V8<T>::rnd(v * sc[j]) : v;
+        for (int v = 0; v < NV; ++v) {
+          const int c = c0 + (v * 32 + lane) * 8;
+          if (c < H) *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(acc[v]);
         }
       }
-    }
-    if constexpr (VEC) {
-      *reinterpret_cast<uint4*>(out + t * ldo + c) = V8<T>::store(acc);
     } else {
-      out[t * ldo + c] = V8<T>::from_f(acc[0]);
+      for (int c = lane; c < H; c += 32) {
+        float acc = 0.f;
+        for (int j = 0; j < k; ++j) {
+          const int row = __ldg(asg_row + t * k + j);
+          if (row < 0) continue;
+          const float v = V8<T>::to_f(y[row * ldy + c]);
+          acc += (w != nullptr) ? V8<T>::rnd(v * V8<T>::to_f(w[t * k + j])) : v;
+        }
+        orow[c] = V8<T>::from_f(acc);
+      }
     }
   }
   pdl_done();
@@ -249,7 +275,7 @@ __global__ void gather_map_kernel(const int32_t* __restrict__ row_asg, long long
 
 int grid_for(long long work_items, int per_block) {
   long long b = (work_items + per_block - 1) / per_block;
-  const long long cap = static_cast<long long>(num_sms()) * 64;
+  const long long cap = static_cast<long long>(num_sms()) * 32;
   if (b > cap) b = cap;
   if (b < 1) b = 1;
   return static_cast<int>(b);
@@ -283,10 +309,10 @@ int gather_t(const void* x, long long ldx, int H, const int32_t* map, int div, l
   T* op = static_cast<T*>(out);
   if constexpr (sizeof(T) == 2) {
     if (vec)
-      return launch_pdl(gather_rows_kernel<T, true>, grid_for(rows * (H / 8), kThreadsPerBlock),
+      return launch_pdl(gather_rows_kernel<T, true>, grid_for(rows, kThreadsPerBlock / 32),
                         st, xp, ldx, H, map, div, rows, rows_dev, wp, op, ldo);
   }
-  return launch_pdl(gather_rows_kernel<T, false>, grid_for(rows * H, kThreadsPerBlock), st, xp,
+  return launch_pdl(gather_rows_kernel<T, false>, grid_for(rows, kThreadsPerBlock / 32), st, xp,
                     ldx, H, map, div, rows, rows_dev, wp, op, ldo);
 }
 
@@ -299,8 +325,8 @@ int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long 
   const T* wp = static_cast<const T*>(w);
   T* op = static_cast<T*>(out);
   // source-row arrays sized to top_k (registers bound the resident blocks)
-  const int grid_v = grid_for(T_tokens * (H / 8), kThreadsPerBlock);
-  const int grid_s = grid_for(T_tokens * H, kThreadsPerBlock);
+  const int grid_v = grid_for(T_tokens, kThreadsPerBlock / 32);
+  const int grid_s = grid_v;
 #define MOE_COMBINE(KM)                                                                       \
   do {                                                                                         \
     if constexpr (sizeof(T) == 2) {                                                            \

@@ -454,7 +454,7 @@ int finalize_tf(const float* part, int nb, int E, long long T, const int32_t* tp
 
 int router_head_blocks(long long T) {
   long long b = (T + kHeadWarps - 1) / kHeadWarps;
-  const long long cap = static_cast<long long>(num_sms());  // few partials to reduce
+  const long long cap = static_cast<long long>(num_sms()) * 4;
   if (b > cap) b = cap;
   if (b < 1) b = 1;
   return static_cast<int>(b);

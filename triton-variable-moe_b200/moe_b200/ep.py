@@ -106,6 +106,7 @@ class _EPPlan:
 class _EPMoEFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_flat, w1, w2, weights, selected, plan: _EPPlan):
+        ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         T, H = x_flat.shape
         k, E = plan.top_k, plan.num_experts
         dev, dt = x_flat.device, x_flat.dtype
@@ -159,6 +160,8 @@ class _EPMoEFunction(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_out, _g_tpe):
+        if grad_out is None:
+            return None, None, None, None, None, None
         (xg, h, pre, weights, w1, w2, r2a, a2r, lr2a, la2r, ltok) = ctx.saved_tensors
         plan = ctx.plan
         lp = plan.local

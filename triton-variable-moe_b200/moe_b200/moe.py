@@ -75,6 +75,7 @@ class _MoEMLPFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x_flat, w1, w2, weights, selected, plan: _Plan):
+        ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         T, H = x_flat.shape
         E, k = plan.num_experts, plan.top_k
         r = _ops.route(selected, E, plan.block_size, "up")
@@ -107,6 +108,8 @@ class _MoEMLPFunction(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_out, _grad_tpe):
+        if grad_out is None:
+            return None, None, None, None, None, None
         xg, h, pre, weights, w1, w2, r2a, a2r, tok_off = ctx.saved_tensors
         plan = ctx.plan
         E, k, cap = plan.num_experts, plan.top_k, ctx.cap
@@ -145,6 +148,7 @@ class _RouterHead(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, logits, top_k, normalize, weights_dtype, widths_normalized):
+        ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         probs, w, sel, lse, ws = _ops.router_head(logits, top_k, normalize, weights_dtype,
                                                   widths_normalized)
         ctx.save_for_backward(probs)
@@ -170,6 +174,7 @@ class _AuxLosses(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, probs, lse, ws, tokens_per_expert, lb_coef, widths_normalized,
                 f_dtype):
+        ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         T = logits.shape[0]
         losses, f_i, _p_i = _ops.aux_losses(ws, T, tokens_per_expert, lb_coef, logits.dtype,
                                             f_dtype)
