@@ -7,12 +7,13 @@
 // (triton_moe/kernels/grouped_gemm.py:104-149) without any host sync.
 //
 // Work is split into "units": contiguous runs of assignments, one warp each.
-//   count   : per-unit per-expert histogram             -> ws[unit][E]
-//   scan    : one CTA; per-expert exclusive scan over units, expert totals,
-//             rounding, bins / padded_bins / offsets, padding-row markers
-//   scatter : per unit, warp-synchronous stable ranks (match_any), writes the
-//             sorted order and both row maps
-// Problems of at most 8192 assignments run all three phases in one CTA.
+//   count        : per-unit per-expert histogram          -> ws[unit][E]
+//   scan+scatter : every block derives its units' starting ranks, the expert
+//                  totals, rounding and offsets from the histograms itself
+//                  (block 0 also writes the per-expert outputs and padding-row
+//                  markers), then each warp ranks its unit stably (match_any)
+//                  and writes the sorted order and both row maps
+// Problems of at most 8192 assignments run all phases in one CTA.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -111,135 +112,137 @@ __device__ int block_excl_scan(int v, int* total) {
   return res;
 }
 
-// ---- phase 2: totals, rounding, offsets, per-unit bases, padding markers ------
-// Launched with one CTA of 1024 threads.  ws[unit][e] becomes the rank of the
-// unit's first assignment to expert e among all assignments to e.
-__global__ void route_scan_kernel(long long units, int E, int bs, int mode, int32_t* ws,
-                                  RouteOut o) {
+// ---- phase 2: scan + stable scatter ------------------------------------------------
+// Every block (8 warps = 8 units) computes what it needs from the per-unit
+// histograms itself: each expert's total and the count of its assignments in
+// units before the block (threads split the units of an expert between them),
+// the expert-level rounding and cumulative sums, and its warps' starting
+// ranks.  Block 0 also writes the per-expert outputs and marks padding rows.
+// Then each warp ranks its unit's assignments stably (match_any) and scatters
+// them.
+template <typename S>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    route_scan_scatter_kernel(const S* __restrict__ sel, long long A, int E, int bs, int mode,
+                              long long U, long long units, const int32_t* __restrict__ ws,
+                              RouteOut o) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  __shared__ int s_n[kMaxE], s_kept[kMaxE], s_pstart[kMaxE], s_padpre[kMaxE + 1];
-  const int tid = threadIdx.x;
-  // per-expert exclusive scan over units: 4 threads per expert column
-  // (E <= 256), each owning a contiguous quarter of the units.
-  constexpr int kParts = 4;
-  const int e = tid % kMaxE, part = tid / kMaxE;
-  const long long per = (units + kParts - 1) / kParts;
-  const long long ub = part * per, ue = min(units, ub + per);
-  int partial = 0;
-  if (e < E)
-    for (long long u = ub; u < ue; ++u) partial += ws[u * E + e];
-  __shared__ int s_part[kParts][kMaxE];
-  s_part[part][e] = partial;
-  __syncthreads();
-  if (e < E) {
-    int run = 0;
-    for (int p = 0; p < part; ++p) run += s_part[p][e];
-    for (long long u = ub; u < ue; ++u) {
-      const int c = ws[u * E + e];
-      ws[u * E + e] = run;
-      run += c;
+  __shared__ int base[kWarpsPerBlock][kMaxE];
+  __shared__ int s_tot[kMaxE], s_before[kMaxE];
+  __shared__ int s_bstart[kMaxE], s_pstart[kMaxE], s_kept[kMaxE], s_padpre[kMaxE + 1];
+  __shared__ int s_part[kWarpsPerBlock * 32], s_part2[kWarpsPerBlock * 32];
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int nthr = kWarpsPerBlock * 32;
+  const long long u0 = static_cast<long long>(blockIdx.x) * kWarpsPerBlock;
+  // (a) per-expert totals and counts before this block's first unit
+  const int parts = max(1, nthr / E);
+  const int groups = nthr / parts;
+  for (int e0 = 0; e0 < E; e0 += groups) {
+    const int g = tid / parts, part = tid % parts;
+    const int e = e0 + g;
+    int tot = 0, bef = 0;
+    if (g < groups && e < E) {
+      for (long long u = part; u < units; u += parts) {
+        const int c = ws[u * E + e];
+        tot += c;
+        if (u < u0) bef += c;
+      }
     }
-    if (part == kParts - 1) {
-      s_n[e] = run;
+    s_part[tid] = tot;
+    s_part2[tid] = bef;
+    __syncthreads();
+    if (g < groups && e < E && part == 0) {
+      int t2 = 0, b2 = 0;
+      for (int q = 0; q < parts; ++q) {
+        t2 += s_part[tid + q];
+        b2 += s_part2[tid + q];
+      }
+      s_tot[e] = t2;
+      s_before[e] = b2;
+    }
+    __syncthreads();
+  }
+  // (b) starting rank of each warp's unit per expert
+  for (int e = tid; e < E; e += nthr) {
+    int run = s_before[e];
+    for (int ww = 0; ww < kWarpsPerBlock; ++ww) {
+      base[ww][e] = run;
+      if (u0 + ww < units) run += ws[(u0 + ww) * E + e];
     }
   }
-  __syncthreads();
-  // expert-level values and the two cumulative sums (threads 0..255 hold experts)
+  // (c) expert level: rounding and the cumulative sums (thread e holds expert e)
   int n = 0, r = 0, kept = 0, pads = 0;
   if (tid < E) {
-    n = s_n[tid];
+    n = s_tot[tid];
     r = rounded_count(n, bs, mode);
     kept = min(n, r);
     pads = r - kept;
   }
   int tot_kept, tot_round, tot_pad;
-  const int kept_ex = block_excl_scan(tid < kMaxE ? kept : 0, &tot_kept);
-  const int round_ex = block_excl_scan(tid < kMaxE ? r : 0, &tot_round);
-  const int pad_ex = block_excl_scan(tid < kMaxE ? pads : 0, &tot_pad);
+  const int kept_ex = block_excl_scan(kept, &tot_kept);
+  const int round_ex = block_excl_scan(r, &tot_round);
+  const int pad_ex = block_excl_scan(pads, &tot_pad);
   if (tid < E) {
     s_kept[tid] = kept;
     s_pstart[tid] = round_ex;
+    s_bstart[tid] = kept_ex;
     s_padpre[tid] = pad_ex;
-    o.tpe[tid] = n;
-    o.bins[tid] = kept_ex + kept;
-    o.padded_bins[tid] = round_ex + r;
-    o.tok_off[tid] = round_ex;
-    o.ptpe[tid] = r;
-    if (tid == E - 1) o.tok_off[E] = round_ex + r;
+    if (blockIdx.x == 0) {
+      o.tpe[tid] = n;
+      o.bins[tid] = kept_ex + kept;
+      o.padded_bins[tid] = round_ex + r;
+      o.tok_off[tid] = round_ex;
+      o.ptpe[tid] = r;
+      if (tid == E - 1) o.tok_off[E] = round_ex + r;
+    }
   }
-  if (tid == 0) s_padpre[E] = tot_pad;
   __syncthreads();
-  if (o.row_asg != nullptr) {
-    if (static_cast<long long>(tot_round) > o.p_cap) {
-      if (tid == 0 && o.status) atomicExch(o.status, kStatusCapacity);
-    } else {
-      // mark padding rows with -1: flatten all pads and binary-search the expert
-      for (int p = tid; p < tot_pad; p += blockDim.x) {
+  const bool write_rows = o.row_asg != nullptr && static_cast<long long>(tot_round) <= o.p_cap;
+  if (blockIdx.x == 0) {
+    if (o.row_asg != nullptr && !write_rows && tid == 0 && o.status)
+      atomicExch(o.status, kStatusCapacity);
+    if (write_rows) {
+      for (int p = tid; p < tot_pad; p += nthr) {
         int lo = 0, hi = E - 1;
         while (lo < hi) {
-          int mid = (lo + hi + 1) >> 1;
+          const int mid = (lo + hi + 1) >> 1;
           if (s_padpre[mid] <= p) lo = mid;
           else hi = mid - 1;
         }
-        const int row = s_pstart[lo] + s_kept[lo] + (p - s_padpre[lo]);
-        o.row_asg[row] = -1;
+        o.row_asg[s_pstart[lo] + s_kept[lo] + (p - s_padpre[lo])] = -1;
       }
     }
   }
-}
-
-// ---- phase 3: stable scatter ---------------------------------------------------
-template <typename S>
-__global__ void route_scatter_kernel(const S* __restrict__ sel, long long A, int E, long long U,
-                                     long long units, const int32_t* __restrict__ ws,
-                                     RouteOut o) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // (d) stable scatter of this warp's unit
+  const long long unit = u0 + w;
+  if (unit < units) {
+    const long long beg = unit * U, end = min(A, beg + U);
+    for (long long i0 = beg; i0 < end; i0 += 32) {
+      const long long i = i0 + lane;
+      const bool valid = i < end;
+      const int e = valid ? load_expert(sel, i, E, nullptr) : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank_in = __popc(peers & ((1u << lane) - 1u));
+      if (e >= 0) {
+        const int rank = base[w][e] + rank_in;
+        if (rank < s_kept[e]) {
+          const int pos = s_bstart[e] + rank;
+          o.bin_ids[pos] = e;
+          o.indices[pos] = static_cast<int32_t>(i);
+          const int row = s_pstart[e] + rank;
+          if (write_rows) o.row_asg[row] = static_cast<int32_t>(i);
+          if (o.asg_row) o.asg_row[i] = row;
+        } else if (o.asg_row) {
+          o.asg_row[i] = -1;  // dropped by "down"/"nearest" rounding
+        }
+      } else if (valid && o.asg_row) {
+        o.asg_row[i] = -1;
+      }
+      __syncwarp();
+      if (e >= 0 && lane == 31 - __clz(peers)) base[w][e] += __popc(peers);
+      __syncwarp();
+    }
+  }
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  __shared__ int base[kWarpsPerBlock][kMaxE];
-  __shared__ int s_bstart[kMaxE], s_pstart[kMaxE], s_kept[kMaxE];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int b_end = o.bins[e];
-    const int b_prev = e > 0 ? o.bins[e - 1] : 0;
-    s_bstart[e] = b_prev;
-    s_kept[e] = b_end - b_prev;
-    s_pstart[e] = o.tok_off[e];
-  }
-  const long long unit = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + w;
-  if (unit < units)
-    for (int e = lane; e < E; e += 32) base[w][e] = ws[unit * E + e];
-  __syncthreads();
-  if (unit >= units) return;
-  const bool write_rows =
-      o.row_asg != nullptr && static_cast<long long>(o.tok_off[E]) <= o.p_cap;
-  const long long beg = unit * U, end = min(A, beg + U);
-  for (long long i0 = beg; i0 < end; i0 += 32) {
-    const long long i = i0 + lane;
-    const bool valid = i < end;
-    const int e = valid ? load_expert(sel, i, E, nullptr) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank_in = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0) {
-      const int rank = base[w][e] + rank_in;
-      if (rank < s_kept[e]) {
-        const int pos = s_bstart[e] + rank;
-        o.bin_ids[pos] = e;
-        o.indices[pos] = static_cast<int32_t>(i);
-        const int row = s_pstart[e] + rank;
-        if (write_rows) o.row_asg[row] = static_cast<int32_t>(i);
-        if (o.asg_row) o.asg_row[i] = row;
-      } else if (o.asg_row) {
-        o.asg_row[i] = -1;  // dropped by "down"/"nearest" rounding
-      }
-    } else if (valid && o.asg_row) {
-      o.asg_row[i] = -1;
-    }
-    __syncwarp();
-    const int leader = 31 - __clz(peers);
-    if (e >= 0 && lane == leader) base[w][e] += __popc(peers);
-    __syncwarp();
-  }
 }
 
 // ---- single-CTA path for small problems ------------------------------------------
@@ -414,10 +417,9 @@ static int route_impl(const S* sel, long long A, int E, int bs, int mode, const 
   const int blocks = static_cast<int>((units + kWarpsPerBlock - 1) / kWarpsPerBlock);
   int rc = launch_pdl(route_count_kernel<S>, blocks, kWarpsPerBlock * 32, 0, st, sel, A, E, U, units,
                       w, o.status);
-  if (rc == kStatusOk) rc = launch_pdl(route_scan_kernel, 1, 1024, 0, st, units, E, bs, mode, w, o);
   if (rc == kStatusOk)
-    rc = launch_pdl(route_scatter_kernel<S>, blocks, kWarpsPerBlock * 32, 0, st, sel, A, E, U, units,
-                    static_cast<const int32_t*>(w), o);
+    rc = launch_pdl(route_scan_scatter_kernel<S>, blocks, kWarpsPerBlock * 32, 0, st, sel, A, E,
+                    bs, mode, U, units, static_cast<const int32_t*>(w), o);
   if (rc != kStatusOk) return rc;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }

@@ -329,8 +329,19 @@ __global__ void __launch_bounds__(256)
     const int e = e0 + tid / parts;
     const int part = tid % parts;
     float v = 0.f;
-    if (e < E && tid / parts < 256 / parts)
-      for (int b = part; b < nblocks; b += parts) v += partials[static_cast<long long>(b) * stride + e];
+    if (e < E && tid / parts < 256 / parts) {
+      // four independent accumulators keep four loads in flight
+      float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
+      int b = part;
+      for (; b + 3 * parts < nblocks; b += 4 * parts) {
+        v0 += partials[static_cast<long long>(b) * stride + e];
+        v1 += partials[static_cast<long long>(b + parts) * stride + e];
+        v2 += partials[static_cast<long long>(b + 2 * parts) * stride + e];
+        v3 += partials[static_cast<long long>(b + 3 * parts) * stride + e];
+      }
+      for (; b < nblocks; b += parts) v0 += partials[static_cast<long long>(b) * stride + e];
+      v = (v0 + v1) + (v2 + v3);
+    }
     s_part[tid] = v;
     __syncthreads();
     if (part == 0 && e < E && tid / parts < 256 / parts) {
@@ -454,7 +465,7 @@ int finalize_tf(const float* part, int nb, int E, long long T, const int32_t* tp
 
 int router_head_blocks(long long T) {
   long long b = (T + kHeadWarps - 1) / kHeadWarps;
-  const long long cap = static_cast<long long>(num_sms()) * 4;
+  const long long cap = static_cast<long long>(num_sms()) * 2;
   if (b > cap) b = cap;
   if (b < 1) b = 1;
   return static_cast<int>(b);

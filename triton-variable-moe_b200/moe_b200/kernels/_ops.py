@@ -30,7 +30,7 @@ _GEMM_DTYPES = (torch.bfloat16, torch.float16)
 _status_bufs: dict[int, torch.Tensor] = {}
 
 # Number of CUDA kernels launched through this module (host-side count; the
-# routing entry point launches one or three).  bench.py reports it per timed region.
+# routing entry point launches one or two).  bench.py reports it per timed region.
 launch_count = 0
 
 
@@ -146,7 +146,7 @@ def route(
     )
     _ev_end(ev, "route")
     check(rc, "moe_route")
-    _count(1 if A <= 8192 else 3)  # one fused CTA for small problems
+    _count(1 if A <= 8192 else 2)  # one fused CTA for small problems
     return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
 
 
