@@ -134,7 +134,8 @@ MOE_API int moe_router_topk(const float* router_probs, int64_t num_tokens, int n
  * moe_aux_losses then forms losses[0] = router_z_loss (mean lse^2, rounded to
  * the logits dtype), losses[1] = load_balance_loss = sum_e lb_coef[e] * f_i[e]
  * * p_i[e], losses[2] = compute_loss = mean_t sum_e probs * widths_normalized,
- * f_i [E] = tokens_per_expert / sum (f_dtype) and p_i [E] fp32 = mean probs.
+ * f_i [E] = tokens_per_expert / sum (f_dtype) and p_i [E] fp32 = mean probs;
+ * z_loss (nullable) receives router_z_loss in the logits dtype.
  */
 MOE_API int64_t moe_router_head_workspace_floats(int64_t num_tokens, int num_experts);
 MOE_API int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tokens,
@@ -145,7 +146,7 @@ MOE_API int moe_router_head(const void* router_logits, int logits_dtype, int64_t
 MOE_API int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,
                            const int32_t* tokens_per_expert, const float* lb_coef,
                            int logits_dtype, float* losses, void* f_i, int f_dtype, float* p_i,
-                           void* stream);
+                           void* z_loss, void* stream);
 
 /*
  * Padded-row maps from the reference's sorted-order metadata (indices,

@@ -28,7 +28,7 @@ int router_head(const void* logits, int l_dtype, long long T, int E, int k, int 
                 float* lse, float* partials, int nblocks, cudaStream_t st);
 int aux_finalize(const float* partials, int nblocks, int E, long long T, const int32_t* tpe,
                  const float* lb_coef, int l_dtype, float* losses, void* f_i, int f_dtype,
-                 float* p_i, cudaStream_t st);
+                 float* p_i, void* z_out, cudaStream_t st);
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
                 long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
                 int dtype, cudaStream_t st);
@@ -154,10 +154,11 @@ int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tok
 
 int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,
                    const int32_t* tokens_per_expert, const float* lb_coef, int logits_dtype,
-                   float* losses, void* f_i, int f_dtype, float* p_i, void* stream) {
+                   float* losses, void* f_i, int f_dtype, float* p_i, void* z_loss,
+                   void* stream) {
   return moe::aux_finalize(workspace, moe::router_head_blocks(num_tokens), num_experts,
                            num_tokens, tokens_per_expert, lb_coef, logits_dtype, losses, f_i,
-                           f_dtype, p_i, S(stream));
+                           f_dtype, p_i, z_loss, S(stream));
 }
 
 int moe_build_row_map(const int32_t* indices, const int32_t* bin_ids, const int32_t* bins,

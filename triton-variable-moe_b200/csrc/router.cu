@@ -315,7 +315,8 @@ template <typename L, typename TF>
 __global__ void __launch_bounds__(256)
     aux_finalize_kernel(const float* __restrict__ partials, int nblocks, int E, long long T,
                         const int32_t* __restrict__ tpe, const float* __restrict__ lb_coef,
-                        float* __restrict__ losses, TF* __restrict__ f_i, float* __restrict__ p_i) {
+                        float* __restrict__ losses, TF* __restrict__ f_i, float* __restrict__ p_i,
+                        L* __restrict__ z_out) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_part[256];
   __shared__ float s_pe[256];
@@ -391,6 +392,7 @@ __global__ void __launch_bounds__(256)
   }
   if (tid == 0) {
     losses[0] = rnd<L>(zsum * invT);
+    if (z_out != nullptr) *z_out = from_float<L>(zsum * invT);
     losses[1] = s_red[0];
     losses[2] = csum * invT;
   }
@@ -435,7 +437,8 @@ int head_tw(const void* logits, long long T, int E, int k, int norm, const float
 
 template <typename L, typename TF>
 int launch_finalize(const float* part, int nb, int E, long long T, const int32_t* tpe,
-                    const float* coef, float* losses, void* f_i, float* p_i, cudaStream_t st) {
+                    const float* coef, float* losses, void* f_i, float* p_i, void* z_out,
+                    cudaStream_t st) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -446,18 +449,18 @@ int launch_finalize(const float* part, int nb, int E, long long T, const int32_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, aux_finalize_kernel<L, TF>, part, nb, E, T, tpe, coef, losses,
-                         static_cast<TF*>(f_i), p_i) != cudaSuccess)
+                         static_cast<TF*>(f_i), p_i, static_cast<L*>(z_out)) != cudaSuccess)
     return kStatusCuda;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }
 
 template <typename L>
 int finalize_tf(const float* part, int nb, int E, long long T, const int32_t* tpe,
-                const float* coef, float* losses, void* f_i, int f_dtype, float* p_i,
+                const float* coef, float* losses, void* f_i, int f_dtype, float* p_i, void* z_out,
                 cudaStream_t st) {
-  if (f_dtype == 0) return launch_finalize<L, __nv_bfloat16>(part, nb, E, T, tpe, coef, losses, f_i, p_i, st);
-  if (f_dtype == 1) return launch_finalize<L, __half>(part, nb, E, T, tpe, coef, losses, f_i, p_i, st);
-  if (f_dtype == 2) return launch_finalize<L, float>(part, nb, E, T, tpe, coef, losses, f_i, p_i, st);
+  if (f_dtype == 0) return launch_finalize<L, __nv_bfloat16>(part, nb, E, T, tpe, coef, losses, f_i, p_i, z_out, st);
+  if (f_dtype == 1) return launch_finalize<L, __half>(part, nb, E, T, tpe, coef, losses, f_i, p_i, z_out, st);
+  if (f_dtype == 2) return launch_finalize<L, float>(part, nb, E, T, tpe, coef, losses, f_i, p_i, z_out, st);
   return kStatusUnsupported;
 }
 
@@ -485,11 +488,11 @@ int router_head(const void* logits, int l_dtype, long long T, int E, int k, int 
 
 int aux_finalize(const float* partials, int nblocks, int E, long long T, const int32_t* tpe,
                  const float* lb_coef, int l_dtype, float* losses, void* f_i, int f_dtype,
-                 float* p_i, cudaStream_t st) {
+                 float* p_i, void* z_out, cudaStream_t st) {
   if (E <= 0 || E > 256 || T <= 0 || nblocks <= 0) return kStatusBadArg;
-  if (l_dtype == 0) return finalize_tf<__nv_bfloat16>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, st);
-  if (l_dtype == 1) return finalize_tf<__half>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, st);
-  if (l_dtype == 2) return finalize_tf<float>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, st);
+  if (l_dtype == 0) return finalize_tf<__nv_bfloat16>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, z_out, st);
+  if (l_dtype == 1) return finalize_tf<__half>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, z_out, st);
+  if (l_dtype == 2) return finalize_tf<float>(partials, nblocks, E, T, tpe, lb_coef, losses, f_i, f_dtype, p_i, z_out, st);
   return kStatusUnsupported;
 }
 

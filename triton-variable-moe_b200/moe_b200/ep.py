@@ -243,9 +243,12 @@ class ExpertParallelMoEMLP(nn.Module):
                              persistent=False)
         self.register_buffer("expert_widths_normalized", full.expert_widths_normalized.clone(),
                              persistent=False)
-        self.register_buffer("_lb_coef", full._lb_coef.clone(), persistent=False)
+        self._lb_coef_values = full._lb_coef_values
         self._local_widths = lw
         self._plan_cache: _EPPlan | None = None
+
+    def _lb_coef(self, device) -> torch.Tensor:
+        return TritonMoEMLP._lb_coef(self, device)
 
     def _slice(self, w1_full: torch.Tensor, w2_full: torch.Tensor):
         offs = [0]
@@ -303,12 +306,12 @@ class ExpertParallelMoEMLP(nn.Module):
         B, S, H = x.shape
         x_flat = x.reshape(B * S, H)
         logits = self.router(x_flat)
+        wn = self.expert_widths_normalized.float()
         probs, w, sel, lse, ws = _RouterHead.apply(logits, self.num_active_experts,
-                                                   self.norm_topk_prob, x_flat.dtype,
-                                                   self.expert_widths_normalized)
+                                                   self.norm_topk_prob, x_flat.dtype, wn)
         out_flat, tpe = _EPMoEFunction.apply(x_flat.to(self.w1.dtype), self.w1, self.w2,
                                              w.reshape(-1), sel.reshape(-1), self._plan())
         z, lb, cl, f_i = _AuxLosses.apply(logits, probs, lse, ws, tpe.to(torch.int32),
-                                          self._lb_coef, self.expert_widths_normalized, x.dtype)
+                                          self._lb_coef(logits.device), wn, x.dtype)
         aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
         return out_flat.reshape(B, S, -1), aux, f_i

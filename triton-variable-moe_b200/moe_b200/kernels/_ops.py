@@ -195,21 +195,23 @@ def router_head(router_logits: torch.Tensor, top_k: int, normalize: bool,
 
 def aux_losses(ws: torch.Tensor, num_tokens: int, tokens_per_expert: torch.Tensor,
                lb_coef: torch.Tensor, logits_dtype: torch.dtype, f_dtype: torch.dtype):
-    """(losses fp32 [3] = z, load balance, compute; f_i [E]; p_i fp32 [E])."""
+    """(losses fp32 [3] = z, load balance, compute; f_i [E]; p_i fp32 [E];
+    z-loss in the logits dtype)."""
     dev = ws.device
     E = tokens_per_expert.numel()
     losses = torch.empty(3, dtype=torch.float32, device=dev)
+    z = torch.empty((), dtype=logits_dtype, device=dev)
     f_i = torch.empty(E, dtype=f_dtype, device=dev)
     p_i = torch.empty(E, dtype=torch.float32, device=dev)
     ev = _ev_begin()
     rc = lib.moe_aux_losses(ptr(ws), int(num_tokens), E, ptr(_meta(tokens_per_expert)),
                             ptr(lb_coef.float().contiguous()), DTYPE_CODE[logits_dtype],
-                            ptr(losses), ptr(f_i), DTYPE_CODE[f_dtype], ptr(p_i),
+                            ptr(losses), ptr(f_i), DTYPE_CODE[f_dtype], ptr(p_i), ptr(z),
                             stream_handle(dev))
     _ev_end(ev, "aux_losses")
     check(rc, "moe_aux_losses")
     _count(1)
-    return losses, f_i, p_i
+    return losses, f_i, p_i, z
 
 
 def build_row_map(

@@ -176,9 +176,8 @@ class _AuxLosses(torch.autograd.Function):
                 f_dtype):
         ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         T = logits.shape[0]
-        losses, f_i, _p_i = _ops.aux_losses(ws, T, tokens_per_expert, lb_coef, logits.dtype,
-                                            f_dtype)
-        z = losses[0].to(logits.dtype)
+        losses, f_i, _p_i, z = _ops.aux_losses(ws, T, tokens_per_expert, lb_coef, logits.dtype,
+                                               f_dtype)
         lb = losses[1]
         cl = losses[2]
         ctx.save_for_backward(logits, lse, f_i, lb_coef, widths_normalized)
@@ -287,7 +286,8 @@ class TritonMoEMLP(nn.Module):
                 (group_sizes[g] / self._num_valid_groups) if g >= 0 else 0.0
                 for g in expert_to_group
             ]
-        self.register_buffer("_lb_coef", torch.tensor(coef, dtype=torch.float32), persistent=False)
+        # kept out of the module's buffers so that module.to(dtype) does not round it
+        self._lb_coef_values = coef
         self._plan_cache: _Plan | None = None
 
     # ------------------------------------------------------------------ helpers
@@ -302,17 +302,40 @@ class TritonMoEMLP(nn.Module):
             self._plan_cache = p
         return p
 
+    def _fp32(self, name: str) -> torch.Tensor:
+        """fp32 view of a float buffer (the module may have been cast to bf16, which
+        rounds the buffer like the reference's); cached per buffer version."""
+        buf = getattr(self, name)
+        if buf.dtype == torch.float32:
+            return buf
+        key = (name, buf.data_ptr(), buf.dtype, buf._version)
+        cache = self.__dict__.setdefault("_fp32_cache", {})
+        hit = cache.get(name)
+        if hit is None or hit[0] != key:
+            hit = (key, buf.float())
+            cache[name] = hit
+        return hit[1]
+
+    def _lb_coef(self, device) -> torch.Tensor:
+        cache = self.__dict__.setdefault("_lb_coef_cache", {})
+        t = cache.get(device)
+        if t is None:
+            t = torch.tensor(self._lb_coef_values, dtype=torch.float32, device=device)
+            cache[device] = t
+        return t
+
     def _route_weights(self, x_flat):
         """(logits, probs, top-k weights, selected int32, lse, loss partials)."""
         router_logits = self.router(x_flat)
         router_probs, top_k_weights, selected, lse, ws = _RouterHead.apply(
             router_logits, self.num_active_experts, self.norm_topk_prob, x_flat.dtype,
-            self.expert_widths_normalized)
+            self._fp32("expert_widths_normalized"))
         return router_logits, router_probs, top_k_weights, selected, lse, ws
 
     def _aux_losses(self, router_logits, lse, ws, router_probs, tokens_per_expert, dtype):
         z, lb, cl, f_i = _AuxLosses.apply(router_logits, router_probs, lse, ws, tokens_per_expert,
-                                          self._lb_coef, self.expert_widths_normalized, dtype)
+                                          self._lb_coef(router_logits.device),
+                                          self._fp32("expert_widths_normalized"), dtype)
         aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
         return aux, f_i
 
