@@ -14,8 +14,10 @@
  *     capacity overflow, a bounded wait that gave up);
  *   - return value: MOE_OK, or a negative MOE_ERR_* code for a host-side
  *     argument or launch error.
- * dtype codes: MOE_DTYPE_BF16 / MOE_DTYPE_F16 for the GEMMs; the permutation
- * kernels also take MOE_DTYPE_F32.
+ * dtype codes: MOE_DTYPE_BF16 / MOE_DTYPE_F16 / MOE_DTYPE_F32 everywhere; the
+ * GEMMs run bf16/fp16 operands on the kind::f16 tensor-core MMA and fp32
+ * operands on the kind::tf32 MMA (the reference's default precision for fp32
+ * dots), always with fp32 accumulation.
  */
 #ifndef MOE_B200_H_
 #define MOE_B200_H_

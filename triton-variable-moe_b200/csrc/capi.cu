@@ -51,7 +51,9 @@ using moe::GroupedGemmDesc;
 
 cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
-bool gemm_dtype_ok(int dtype) { return dtype == MOE_DTYPE_BF16 || dtype == MOE_DTYPE_F16; }
+bool gemm_dtype_ok(int dtype) {
+  return dtype == MOE_DTYPE_BF16 || dtype == MOE_DTYPE_F16 || dtype == MOE_DTYPE_F32;
+}
 
 int pick_bn(int tile_n, long long n_hint) {
   if (tile_n == 128 || tile_n == 256) return tile_n;
@@ -374,7 +376,7 @@ Built build_down_dw(const void* inter, int64_t rows, int64_t ld_inter, const voi
 int run1(const Built& b, int dtype, void* stream) {
   if (b.err) return b.err;
   if (!gemm_dtype_ok(dtype)) return MOE_ERR_UNSUPPORTED;
-  return moe::run_grouped_gemm(b.op, b.g, b.epi, dtype == MOE_DTYPE_F16, S(stream));
+  return moe::run_grouped_gemm(b.op, b.g, b.epi, dtype, S(stream));
 }
 
 int run2(const Built& a, const Built& b, int dtype, void* stream) {
@@ -384,7 +386,7 @@ int run2(const Built& a, const Built& b, int dtype, void* stream) {
   const GemmOperands ops[2] = {a.op, b.op};
   const GroupedGemmDesc gs[2] = {a.g, b.g};
   const int epis[2] = {a.epi, b.epi};
-  return moe::run_grouped_gemms(ops, gs, epis, 2, dtype == MOE_DTYPE_F16, S(stream));
+  return moe::run_grouped_gemms(ops, gs, epis, 2, dtype, S(stream));
 }
 
 }  // namespace

@@ -28,14 +28,12 @@ namespace moe {
 namespace {
 
 constexpr int BM = 128;  // UMMA M: one TMEM lane per output row
-constexpr int BK = 64;   // k-block: one 128-byte swizzle row of bf16
-constexpr int UK = 16;   // K per tcgen05.mma (kind::f16)
 constexpr int BN_MAX = 256;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
-constexpr int kABytes = BM * BK * 2;     // 16 KB
+constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-block
 constexpr int kRingBytes = 192 * 1024;   // smem ring for the A/B stages
-constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 128 bytes
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
 constexpr int kSmemBytes = 1024 + kRingBytes + kEpiBytes + 256;
 
@@ -113,6 +111,48 @@ struct Cvt<__half> {
   }
 };
 
+template <>
+struct Cvt<float> {
+  static __device__ __forceinline__ float round(float a) { return a; }
+};
+
+// Per element type: bytes, elements per 128-byte swizzle row (the k-block),
+// elements per MMA K step (32 bytes), elements per 16-byte chunk, and the
+// tcgen05 operand format code.
+template <typename T>
+struct Elem {
+  static constexpr int ES = sizeof(T);
+  static constexpr int BKE = 128 / ES;
+  static constexpr int UKE = 32 / ES;
+  static constexpr int EPC = 16 / ES;
+  static constexpr int FMT = std::is_same<T, float>::value ? 2 : (std::is_same<T, __half>::value ? 0 : 1);
+};
+
+template <typename T>
+__device__ __forceinline__ uint4 pack_chunk(const float* v) {
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = __float_as_uint(v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = Cvt<T>::pack(v[2 * i], v[2 * i + 1]);
+  }
+  return o;
+}
+template <typename T>
+__device__ __forceinline__ void unpack_chunk(const uint4& u, float* v) {
+  const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(up[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) Cvt<T>::unpack(up[i], v[2 * i], v[2 * i + 1]);
+  }
+}
+
 struct Tile {
   int p, e, m0, n0, slot;
 };
@@ -141,8 +181,10 @@ __device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& 
 // bit 1 = B MN-major, bit 2 = N tile 256 (else 128).
 constexpr int cfg_of(int a_mn, int b_mn, int bn) { return a_mn | (b_mn << 1) | ((bn == 256) << 2); }
 
-// Producer side of one tile: stream its k-blocks into the smem ring.
-template <int CFG>
+// Producer side of one tile: stream its k-blocks into the smem ring.  A tile
+// is 128 rows (A) / NT rows (B) of one 128-byte swizzle row of K each; an
+// MN-major operand arrives as 128-byte-wide MN blocks, one box each.
+template <int CFG, typename T>
 __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint64_t* full,
                                              uint64_t* empty, volatile int* abort_flag,
                                              const void* tA, const void* tB, int nkb, int am,
@@ -150,23 +192,25 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
                                              uint32_t& phase) {
   constexpr bool A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = (CFG & 4) ? 256 : 128;
-  constexpr uint32_t bytes = kABytes + NT * BK * 2;
+  constexpr int BKE = Elem<T>::BKE;
+  constexpr uint32_t bytes = kABytes + NT * 128;
   for (int kb = 0; kb < nkb; ++kb) {
     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
     mbar_arrive_expect_tx(&full[stage], bytes);
     uint8_t* a_dst = ring + stage * SB;
     uint8_t* b_dst = a_dst + kABytes;
-    const int kc = kb * BK;
+    const int kc = kb * BKE;
     if constexpr (A_MN) {
-      tma_load_2d(a_dst, tA, &full[stage], am, ak + kc);
-      tma_load_2d(a_dst + 8192, tA, &full[stage], am + 64, ak + kc);
+#pragma unroll
+      for (int j = 0; j < BM / BKE; ++j)
+        tma_load_2d(a_dst + j * BKE * 128, tA, &full[stage], am + BKE * j, ak + kc);
     } else {
       tma_load_2d(a_dst, tA, &full[stage], ak + kc, am);
     }
     if constexpr (B_MN) {
 #pragma unroll
-      for (int j = 0; j < NT / 64; ++j)
-        tma_load_2d(b_dst + j * 8192, tB, &full[stage], bn + 64 * j, bk + kc);
+      for (int j = 0; j < NT / BKE; ++j)
+        tma_load_2d(b_dst + j * BKE * 128, tB, &full[stage], bn + BKE * j, bk + kc);
     } else {
       tma_load_2d(b_dst, tB, &full[stage], bk + kc, bn);
     }
@@ -179,33 +223,35 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
 }
 
 // MMA side of one tile: issue its k-blocks into the TMEM accumulator.
-template <int CFG, int F16>
+template <int CFG, typename T>
 __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t* full,
                                          uint64_t* empty, volatile int* abort_flag,
                                          uint32_t d_tmem, int K, int nkb, int& stage,
                                          uint32_t& phase) {
   constexpr int A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = (CFG & 4) ? 256 : 128;
-  constexpr uint32_t idesc = idesc_f16(BM, NT, A_MN, B_MN, F16);
-  constexpr uint32_t a_step = A_MN ? 2048u : 32u, a_lbo = A_MN ? 8192u : 16u;
-  constexpr uint32_t b_step = B_MN ? 2048u : 32u, b_lbo = B_MN ? 8192u : 16u;
+  constexpr int BKE = Elem<T>::BKE, UKE = Elem<T>::UKE;
+  constexpr uint32_t idesc = idesc_mma(BM, NT, A_MN, B_MN, Elem<T>::FMT);
+  // K-major: the next K step is 32 bytes further along the swizzled row.
+  // MN-major: it is UKE rows (of 128 bytes) further; MN blocks are LBO apart.
+  constexpr uint32_t a_step = A_MN ? UKE * 128u : 32u, a_lbo = A_MN ? BKE * 128u : 16u;
+  constexpr uint32_t b_step = B_MN ? UKE * 128u : 32u, b_lbo = B_MN ? BKE * 128u : 16u;
+  // MN-major fp32 tiles use the 32-byte-granular swizzle: 4-row K groups.
+  constexpr bool kW = sizeof(T) == 4;
+  constexpr uint32_t a_sbo = (A_MN && kW) ? 512u : 1024u, a_lay = (A_MN && kW) ? 1u : 2u;
+  constexpr uint32_t b_sbo = (B_MN && kW) ? 512u : 1024u, b_lay = (B_MN && kW) ? 1u : 2u;
   for (int kb = 0; kb < nkb; ++kb) {
     if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
     tc_fence_after();
     const uint32_t a_addr = smem_u32(ring + stage * SB);
     const uint32_t b_addr = a_addr + kABytes;
-    const int nk = min(BK, K - kb * BK) / UK;
-    if (nk == BK / UK) {
-#pragma unroll
-      for (int kk = 0; kk < BK / UK; ++kk)
-        tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + kk * a_step, a_lbo, 1024),
-                   smem_desc_sw128(b_addr + kk * b_step, b_lbo, 1024), idesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
-    } else {
-      for (int kk = 0; kk < nk; ++kk)
-        tc_mma_f16(d_tmem, smem_desc_sw128(a_addr + kk * a_step, a_lbo, 1024),
-                   smem_desc_sw128(b_addr + kk * b_step, b_lbo, 1024), idesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
+    const int nk = min(BKE, K - kb * BKE) / UKE;
+    for (int kk = 0; kk < nk; ++kk) {
+      const uint64_t ad = smem_desc_sw128(a_addr + kk * a_step, a_lbo, a_sbo, a_lay);
+      const uint64_t bd = smem_desc_sw128(b_addr + kk * b_step, b_lbo, b_sbo, b_lay);
+      const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+      if constexpr (sizeof(T) == 4) tc_mma_tf32(d_tmem, ad, bd, idesc, acc);
+      else tc_mma_f16(d_tmem, ad, bd, idesc, acc);
     }
     tc_commit(&empty[stage]);  // smem stage free once these MMAs retire
     if (++stage == S) {
@@ -291,11 +337,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         K = max(dim_value(g.k_src, e, g), 0);
         // TMA needs 16-byte aligned inner coordinates and the MMA consumes K in
         // steps of 16: reject (and skip) any expert whose geometry breaks that.
-        const bool bad = (K % 16) != 0 || (g.n_src == DIM_WIDTH && N % 16 != 0) ||
+        constexpr int kAlign = 16 / static_cast<int>(sizeof(T));  // elements per 16 bytes
+        const bool bad = (K % Elem<T>::UKE) != 0 || (g.n_src == DIM_WIDTH && N % 16 != 0) ||
                          (g.m_src == DIM_WIDTH && M % 16 != 0) ||
-                         (base_value(g.b_n_base, e, g) % 8) != 0 ||
-                         (base_value(g.b_k_base, e, g) % 8) != 0 ||
-                         (base_value(g.d_n_base, e, g) % 8) != 0;
+                         (base_value(g.b_n_base, e, g) % kAlign) != 0 ||
+                         (base_value(g.b_k_base, e, g) % kAlign) != 0 ||
+                         (base_value(g.d_n_base, e, g) % kAlign) != 0;
         if (bad && g.status != nullptr) atomicExch(g.status, kStatusBadArg);
         const int bn = P.pr[p].bn;
         tiles = (!bad && M > 0 && N > 0) ? ((M + BM - 1) / BM) * ((N + bn - 1) / bn) : 0;
@@ -337,16 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Problem& pr = P.pr[tl.p];
         const GroupedGemmDesc& g = pr.g;
         const int K = tb.K[tl.slot];
-        const int nkb = (K + BK - 1) / BK;
+        const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
         const int am = slot_base(g.a_m_base, tb, tl.slot) + tl.m0;
         const int ak = slot_base(g.a_k_base, tb, tl.slot);
         const int bn = slot_base(g.b_n_base, tb, tl.slot) + tl.n0;
         const int bk = slot_base(g.b_k_base, tb, tl.slot);
         if (tl.p == 0)
-          ok = produce_tile<CFG0>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0], &P.tmB[0],
+          ok = produce_tile<CFG0, T>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0], &P.tmB[0],
                                   nkb, am, ak, bn, bk, stage, phase);
         else
-          ok = produce_tile<CFG1>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1], &P.tmB[1],
+          ok = produce_tile<CFG1, T>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1], &P.tmB[1],
                                   nkb, am, ak, bn, bk, stage, phase);
       }
     }
@@ -362,16 +409,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = decode_tile(tb, P, nge, t);
         const int K = tb.K[tl.slot];
-        const int nkb = (K + BK - 1) / BK;
+        const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN_MAX);
-        constexpr int F16 = std::is_same<T, __half>::value ? 1 : 0;
         if (tl.p == 0)
-          ok = mma_tile<CFG0, F16>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
+          ok = mma_tile<CFG0, T>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
                                    phase);
         else
-          ok = mma_tile<CFG1, F16>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
+          ok = mma_tile<CFG1, T>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
                                    phase);
         if (!ok) break;
         if (nkb > 0) tc_commit(&acc_full[buf]);
@@ -387,11 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Results are
-    // produced one 64-column slab at a time: every lane converts its own row
+    // produced one 128-byte-wide slab (64 bf16 / 32 fp32 columns) at a time: every lane converts its own row
     // into a 32 x 128 B staging tile (16-byte chunks XOR-swizzled by row, so
     // the row-per-lane writes and the row-major reads are bank-conflict free),
     // then the warp stores the slab row-major, four full 128-byte rows per
     // instruction.
+    constexpr int EPC = Elem<T>::EPC;  // elements per 16-byte chunk
+    constexpr int SLAB = 8 * EPC;      // columns per 128-byte staging row
     const int q = warp & 3;
     uint8_t* stg = sEpi + q * 4096;
     int buf = 0;
@@ -428,20 +476,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int it = 0; it < 8; ++it) {
           const int row = it * 4 + rsub;
-          if (row < rows_ok && csub * 8 < cvalid)
-            *reinterpret_cast<uint4*>(dst + (grow0 + row) * ld + gcol0 + s + csub * 8) = sv[it];
+          if (row < rows_ok && csub * EPC < cvalid)
+            *reinterpret_cast<uint4*>(dst + (grow0 + row) * ld + gcol0 + s + csub * EPC) = sv[it];
         }
       };
 #pragma unroll 1
-      for (int s = 0; s < ncols; s += 64) {
-        const int cvalid = min(64, ncols - s);
-        float v[64];
+      for (int s = 0; s < ncols; s += SLAB) {
+        const int cvalid = min(SLAB, ncols - s);
+        float v[SLAB];
         if (K > 0) {
           tmem_ld32(tbase + s, *reinterpret_cast<float(*)[32]>(&v[0]));
-          if (cvalid > 32) tmem_ld32(tbase + s + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+          if constexpr (SLAB > 32)
+            if (cvalid > 32) tmem_ld32(tbase + s + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = 0.f;
+          for (int i = 0; i < SLAB; ++i) v[i] = 0.f;
         }
         if (epi == EPI_DACT) {
           // stage pre (row-major, coalesced; all eight loads in flight first)
@@ -450,28 +499,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int it = 0; it < 8; ++it) {
             const int row = it * 4 + rsub;
             pv[it] = make_uint4(0, 0, 0, 0);
-            if (row < rows_ok && csub * 8 < cvalid)
+            if (row < rows_ok && csub * EPC < cvalid)
               pv[it] = __ldg(reinterpret_cast<const uint4*>(AUX + (grow0 + row) * g.ld_aux +
-                                                            gcol0 + s + csub * 8));
+                                                            gcol0 + s + csub * EPC));
           }
 #pragma unroll
           for (int it = 0; it < 8; ++it) *stg_chunk(it * 4 + rsub, csub) = pv[it];
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint4 p = *stg_chunk(lane, j);
-            const uint32_t* pp = reinterpret_cast<const uint32_t*>(&p);
-            uint4 o;
-            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+            float pr_[EPC], o[EPC];
+            unpack_chunk<T>(*stg_chunk(lane, j), pr_);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float p0, p1;
-              Cvt<T>::unpack(pp[i], p0, p1);
-              const float g0 = Cvt<T>::round(v[j * 8 + 2 * i]);
-              const float g1 = Cvt<T>::round(v[j * 8 + 2 * i + 1]);
-              op[i] = Cvt<T>::pack(p0 > 0.f ? g0 * 2.0f * p0 : 0.f, p1 > 0.f ? g1 * 2.0f * p1 : 0.f);
+            for (int i = 0; i < EPC; ++i) {
+              const float gi = Cvt<T>::round(v[j * EPC + i]);
+              o[i] = pr_[i] > 0.f ? gi * 2.0f * pr_[i] : 0.f;
             }
-            *stg_chunk(lane, j) = o;
+            *stg_chunk(lane, j) = pack_chunk<T>(o);
           }
           __syncwarp();
           store_slab(D, g.ldd, s, cvalid);
@@ -479,30 +523,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           if (epi == EPI_RELU2) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) v[i] = fmaxf(v[i], 0.f);
+            for (int i = 0; i < SLAB; ++i) v[i] = fmaxf(v[i], 0.f);
           }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 o;
-            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) op[i] = Cvt<T>::pack(v[j * 8 + 2 * i], v[j * 8 + 2 * i + 1]);
-            *stg_chunk(lane, j) = o;
-          }
+          for (int j = 0; j < 8; ++j) *stg_chunk(lane, j) = pack_chunk<T>(&v[j * EPC]);
           __syncwarp();
           if (epi == EPI_RELU2) {
             store_slab(AUX, g.ld_aux, s, cvalid);  // pre = relu(acc)
             __syncwarp();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              uint4 o;
-              uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+              float sq[EPC];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float a = v[j * 8 + 2 * i], b = v[j * 8 + 2 * i + 1];
-                op[i] = Cvt<T>::pack(a * a, b * b);
-              }
-              *stg_chunk(lane, j) = o;
+              for (int i = 0; i < EPC; ++i) sq[i] = v[j * EPC + i] * v[j * EPC + i];
+              *stg_chunk(lane, j) = pack_chunk<T>(sq);
             }
             __syncwarp();
           }
@@ -546,18 +580,27 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D row-major tensor [outer, inner] with row stride `ld` elements, 128-byte
 // swizzled boxes of box_inner x box_outer elements.
-int make_tmap(CUtensorMap* tm, const void* base, int is_f16, long long inner, long long outer,
-              long long ld, int box_inner, int box_outer) {
+// dtype: 0 bf16, 1 fp16, 2 fp32.
+// mn_major: the tile feeds the MMA as an MN-major operand; fp32 ones then use
+// the 128B swizzle with 32-byte granules that kind::tf32 reads MN-major.
+int make_tmap(CUtensorMap* tm, const void* base, int dtype, long long inner, long long outer,
+              long long ld, int box_inner, int box_outer, bool mn_major) {
   auto fn = encode_fn();
   if (!fn) return kStatusCuda;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return kStatusBadArg;
+  const int es = dtype == 2 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * es) % 16 != 0) return kStatusBadArg;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, is_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+  const CUtensorMapDataType dt = dtype == 2   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = fn(tm, dt,
                   2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  (dtype == 2 && mn_major) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                           : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? kStatusOk : kStatusBadArg;
 }
@@ -637,8 +680,21 @@ int num_sms() {
   return n;
 }
 
+template <typename T>
+int dispatch(int used, int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
+  if (used == 1) return launch_single<T>(c0, P, grid, st);
+  return launch_pair<T>(c0, c1, P, grid, st);
+}
+
+int dispatch_dtype(int dtype, int used, int c0, int c1, const MultiParams& P, int grid,
+                   cudaStream_t st) {
+  if (dtype == 2) return dispatch<float>(used, c0, c1, P, grid, st);
+  if (dtype == 1) return dispatch<__half>(used, c0, c1, P, grid, st);
+  return dispatch<__nv_bfloat16>(used, c0, c1, P, grid, st);
+}
+
 int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
-                      int is_f16, cudaStream_t st) {
+                      int dtype, cudaStream_t st) {
   if (n <= 0 || n > kMaxProblems) return kStatusBadArg;
   MultiParams P;
   memset(&P, 0, sizeof(P));
@@ -654,11 +710,13 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     int s;
     // A is [a_rows, a_cols] row-major.  K-major A: rows are M, columns are K.
     // MN-major A: rows are K, columns are M.
-    if (op.a_mn) s = make_tmap(&P.tmA[used], op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, 64);
-    else s = make_tmap(&P.tmA[used], op.a, is_f16, op.a_cols, op.a_rows, op.lda, 64, BM);
+    // boxes are one 128-byte swizzle row wide: 64 bf16 / 32 fp32 elements
+    const int bke = dtype == 2 ? 32 : 64;
+    if (op.a_mn) s = make_tmap(&P.tmA[used], op.a, dtype, op.a_cols, op.a_rows, op.lda, bke, bke, true);
+    else s = make_tmap(&P.tmA[used], op.a, dtype, op.a_cols, op.a_rows, op.lda, bke, BM, false);
     if (s) return s;
-    if (op.b_mn) s = make_tmap(&P.tmB[used], op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, 64);
-    else s = make_tmap(&P.tmB[used], op.b, is_f16, op.b_cols, op.b_rows, op.ldb, 64, bn);
+    if (op.b_mn) s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bke, true);
+    else s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bn, false);
     if (s) return s;
     P.pr[used].g = g;
     P.pr[used].a_mn = op.a_mn;
@@ -671,17 +729,13 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   }
   if (used == 0) return kStatusOk;
   P.nprob = used;
-  P.stage_bytes = kABytes + bn_max * BK * 2;
+  P.stage_bytes = kABytes + bn_max * 128;
   P.stages = kRingBytes / P.stage_bytes;
   if (P.stages > kMaxStages) P.stages = kMaxStages;
   if (grid <= 0) grid = num_sms();
   const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn);
-  if (used == 1)
-    return is_f16 ? launch_single<__half>(c0, P, grid, st)
-                  : launch_single<__nv_bfloat16>(c0, P, grid, st);
-  const int c1 = cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn);
-  int rc = is_f16 ? launch_pair<__half>(c0, c1, P, grid, st)
-                  : launch_pair<__nv_bfloat16>(c0, c1, P, grid, st);
+  const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn) : c0;
+  int rc = dispatch_dtype(dtype, used, c0, c1, P, grid, st);
   if (rc != kStatusUnsupported) return rc;
   // no compiled pair for these configurations: one launch per problem
   for (int i = 0; i < used; ++i) {
@@ -690,19 +744,18 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     Q.tmA[0] = P.tmA[i];
     Q.tmB[0] = P.tmB[i];
     Q.pr[0] = P.pr[i];
-    Q.stage_bytes = kABytes + P.pr[i].bn * BK * 2;
+    Q.stage_bytes = kABytes + P.pr[i].bn * 128;
     Q.stages = kRingBytes / Q.stage_bytes > kMaxStages ? kMaxStages : kRingBytes / Q.stage_bytes;
     const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn);
-    rc = is_f16 ? launch_single<__half>(ci, Q, grid, st)
-                : launch_single<__nv_bfloat16>(ci, Q, grid, st);
+    rc = dispatch_dtype(dtype, 1, ci, ci, Q, grid, st);
     if (rc != kStatusOk) return rc;
   }
   return kStatusOk;
 }
 
-int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int is_f16,
+int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int dtype,
                      cudaStream_t st) {
-  return run_grouped_gemms(&op, &g, &epi, 1, is_f16, st);
+  return run_grouped_gemms(&op, &g, &epi, 1, dtype, st);
 }
 
 }  // namespace moe

@@ -31,11 +31,11 @@ struct GemmOperands {
   int grid;  // CTAs; 0 = one per SM
 };
 
-int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int is_f16,
+int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int dtype,
                      cudaStream_t st);
 // Up to kMaxProblems independent grouped GEMMs in one persistent launch.
 int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
-                      int is_f16, cudaStream_t st);
+                      int dtype, cudaStream_t st);  // dtype: 0 bf16, 1 fp16, 2 fp32 (tf32 MMA)
 
 int num_sms();
 

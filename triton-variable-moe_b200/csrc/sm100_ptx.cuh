@@ -127,6 +127,17 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem] for kind::tf32 (fp32 operands read as tf32,
+// fp32 accumulate).
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed (also frees the smem operands they read).
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -156,26 +167,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 // Shared-memory matrix descriptor (tcgen05 format) for a 128-byte-swizzled
-// operand tile.  K-major: rows of 64 bf16 (128 B), 8-row groups SBO apart.
-// MN-major: 64-element MN blocks LBO apart, 8-row K groups SBO apart.
+// operand tile.  K-major: rows of 128 B, 8-row groups SBO apart.  MN-major:
+// 128-byte MN blocks LBO apart, K-row groups SBO apart.  layout 2 is the
+// 16-byte-granular 128B swizzle (8-row atoms); layout 1 is the 128B swizzle
+// with 32-byte granules (4-row atoms), the only MN-major layout of kind::tf32.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo,
-                                                    uint32_t sbo) {
+                                                    uint32_t sbo, uint32_t layout = 2) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
-  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  d |= static_cast<uint64_t>(layout) << 61;  // 2 = SWIZZLE_128B, 1 = SWIZZLE_128B_BASE32B
   return d;
 }
 
-// Instruction descriptor for kind::f16, fp32 accumulator.
-// is_f16: 0 = bf16 operands, 1 = fp16 operands.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn_major, int b_mn_major,
-                                                 int is_f16) {
+// Instruction descriptor for kind::f16 / kind::tf32 with an fp32 accumulator.
+// fmt: operand format code, 0 = fp16, 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32).
+__host__ __device__ constexpr uint32_t idesc_mma(int M, int N, int a_mn_major, int b_mn_major,
+                                                 int fmt) {
   return (1u << 4)                                       // D format: F32
-         | ((is_f16 ? 0u : 1u) << 7)                      // A format
-         | ((is_f16 ? 0u : 1u) << 10)                     // B format
+         | (static_cast<uint32_t>(fmt) << 7)              // A format
+         | (static_cast<uint32_t>(fmt) << 10)             // B format
          | (static_cast<uint32_t>(a_mn_major) << 15)      // A major-ness
          | (static_cast<uint32_t>(b_mn_major) << 16)      // B major-ness
          | (static_cast<uint32_t>(N >> 3) << 17)          // N / 8

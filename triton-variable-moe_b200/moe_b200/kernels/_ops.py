@@ -25,7 +25,7 @@ from .._lib import (
     stream_handle,
 )
 
-_GEMM_DTYPES = (torch.bfloat16, torch.float16)
+_GEMM_DTYPES = (torch.bfloat16, torch.float16, torch.float32)  # fp32 runs on the tf32 MMA
 
 _status_bufs: dict[int, torch.Tensor] = {}
 
@@ -330,7 +330,7 @@ def _gemm_check(*ts: torch.Tensor) -> None:
             raise ValueError("grouped GEMM operands must be row-major contiguous in the last dim")
     if dt not in _GEMM_DTYPES:
         raise NotImplementedError(
-            f"grouped GEMM dtype {dt}: the sm_100a kernels compute in bf16/fp16 with fp32 accumulation"
+            f"grouped GEMM dtype {dt}: the sm_100a kernels take bf16/fp16 (kind::f16) or fp32 (kind::tf32) operands with fp32 accumulation"
         )
 
 
