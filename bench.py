@@ -283,10 +283,12 @@ def build_ep_layer(cfg, device, seed=0):
     return layer.to(device=device, dtype=torch.bfloat16)
 
 
-def capture_step(layer, x, gout):
+def capture_step(layer, x, gout, kernel_events=False):
     """Capture one fwd+bwd of the layer in a CUDA graph (the layer never
     synchronises the host, so the whole step is capturable).  Returns the graph,
-    its static output and how many of our kernels one replay launches."""
+    its static output, how many of our kernels one replay launches and (with
+    kernel_events) the (name, start, end) event pairs recorded around each of
+    our launches inside the graph."""
     import torch
 
     from moe_b200.kernels import _ops
@@ -305,10 +307,16 @@ def capture_step(layer, x, gout):
     x.grad = None
     graph = torch.cuda.CUDAGraph()
     l0 = _ops.launch_count
+    evs: list = []
     with torch.cuda.graph(graph):
-        out, _, _ = layer(x)
-        out.backward(gout)
-    return graph, out, _ops.launch_count - l0
+        if kernel_events:
+            with _ops.record_kernel_events(external=True) as evs:
+                out, _, _ = layer(x)
+                out.backward(gout)
+        else:
+            out, _, _ = layer(x)
+            out.backward(gout)
+    return graph, out, _ops.launch_count - l0, evs
 
 
 # ------------------------------------------------------------------ arms
@@ -396,7 +404,7 @@ def run_b200(args, cfg, name):
         return 0
 
     if ws == 1:
-        graph, out_static, per_step_launches = capture_step(layer, x, gout)
+        graph, out_static, per_step_launches, _ = capture_step(layer, x, gout)
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
@@ -463,13 +471,32 @@ def run_b200(args, cfg, name):
     flops = gemm_flops(tpe, cfg)
     reps = 5
     per_kind: dict[str, float] = {}
-    for _ in range(reps):
-        flush.zero_()
-        with _ops.record_kernel_events() as evs:
-            step(x, gout)
-        torch.cuda.synchronize()
-        for kname, a, b in evs:
-            per_kind[kname] = per_kind.get(kname, 0.0) + a.elapsed_time(b) / reps
+    kernel_timing = "eager"
+    if ws == 1:
+        # the graphed step again, with an event-record node around each of our
+        # launches: device time per kernel without host launch overhead
+        try:
+            tgraph, evs = capture_step(layer, x, gout, kernel_events=True)[::3]
+            for _ in range(2):
+                tgraph.replay()
+            for _ in range(reps):
+                flush.zero_()
+                tgraph.replay()
+                torch.cuda.synchronize()
+                for kname, a, b in evs:
+                    per_kind[kname] = per_kind.get(kname, 0.0) + a.elapsed_time(b) / reps
+            kernel_timing = "graph"
+            del tgraph
+        except RuntimeError:
+            per_kind = {}
+    if not per_kind:
+        for _ in range(reps):
+            flush.zero_()
+            with _ops.record_kernel_events() as evs:
+                step(x, gout)
+            torch.cuda.synchronize()
+            for kname, a, b in evs:
+                per_kind[kname] = per_kind.get(kname, 0.0) + a.elapsed_time(b) / reps
     gemm_ms = sum(v for k, v in per_kind.items() if k.startswith("grouped_gemm"))
     perm_ms = sum(v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
     n_gemm_launches = 4
@@ -502,22 +529,86 @@ def run_b200(args, cfg, name):
     }
     kernel_us = {k: round(v * 1e3, 2) for k, v in sorted(per_kind.items())}
 
-    # end to end through the public API with host buffers (graphed step)
-    out_host = torch.empty(cfg["batch"], cfg["seq"], H, dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step():
+    # End to end through the public API with host buffers.  Every step copies its
+    # inputs (tokens and output gradient) from pinned host memory and reads its
+    # output back to pinned host memory; the copies run on their own streams so
+    # step i's upload and step i-1's download overlap step i's compute (two
+    # device slots).  The L2 flush still precedes each step's compute.
+    if ws == 1:
+        slots = [(x, gout, graph, out_static)]
+        x2 = torch.empty_like(x).requires_grad_(True)
+        g2 = torch.empty_like(gout)
         with torch.no_grad():
-            x.copy_(x_host, non_blocking=True)
-            gout.copy_(g_host, non_blocking=True)
-        if ws == 1:
-            graph.replay()
-            out_host.copy_(out_static.detach(), non_blocking=True)
-        else:
-            out = step(x, gout)
-            out_host.copy_(out.detach(), non_blocking=True)
+            x2.copy_(x)
+            g2.copy_(gout)
+        graph2, out2, _, _ = capture_step(layer, x2, g2)
+        slots.append((x2, g2, graph2, out2))
+    else:
+        x2 = x.detach().clone().requires_grad_(True)
+        slots = [(x, gout, None, None), (x2, gout.clone(), None, None)]
+    out_host = [torch.empty(cfg["batch"], cfg["seq"], H, dtype=torch.bfloat16).pin_memory()
+                for _ in range(2)]
 
-    e2e_ms = timed(e2e_step, args.steps)
+    def e2e_run(n):
+        comp = torch.cuda.current_stream()
+        up, down = torch.cuda.Stream(), torch.cuda.Stream()
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        in_ready = [ev() for _ in range(n)]
+        computed = [ev() for _ in range(n)]
+        fetched = [ev() for _ in range(n)]
+        outs = [None] * n
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(comp)
+
+        def upload(i):
+            xs, gs = slots[i % 2][0], slots[i % 2][1]
+            up.wait_event(t0)
+            if i >= 2:
+                up.wait_event(computed[i - 2])  # the slot's previous step is done with it
+            with torch.cuda.stream(up), torch.no_grad():
+                xs.copy_(x_host, non_blocking=True)
+                gs.copy_(g_host, non_blocking=True)
+                in_ready[i].record(up)
+
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            xs, gs, gr, os_ = slots[i % 2]
+            comp.wait_event(in_ready[i])
+            if i >= 2:
+                comp.wait_event(fetched[i - 2])  # the slot's output was read back
+            flush.zero_()
+            if gr is not None:
+                gr.replay()
+                o = os_
+            else:
+                o = step(xs, gs)
+            outs[i] = o
+            computed[i].record(comp)
+            down.wait_event(computed[i])
+            with torch.cuda.stream(down):
+                out_host[i % 2].copy_(o.detach(), non_blocking=True)
+                fetched[i].record(down)
+        comp.wait_event(fetched[n - 1])
+        t1.record(comp)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        t = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    e2e_run(3)
+    e2e_ms = e2e_run(args.steps)
     e2e_value = T * ws * args.steps / (e2e_ms / 1e3)
+    torch.cuda.synchronize()
+    e2e_ok = bool(torch.equal(out_host[(args.steps - 1) % 2],
+                              slots[(args.steps - 1) % 2][3].detach().cpu())) if ws == 1 else None
     nbytes = x_host.numel() * 2
 
     cpu = None
@@ -552,14 +643,18 @@ def run_b200(args, cfg, name):
             },
             "roofline": roofline,
             "permute_roofline": permute,
-            "kernel_us_per_step_eager": kernel_us,
+            "kernel_us_per_step": kernel_us,
+            "kernel_timing": kernel_timing,
             "eager_ms_per_step": eager_ms,
             "execution": ("step captured once in a CUDA graph and replayed (eager time in "
                           "eager_ms_per_step)") if ws == 1 else
                          "eager (expert-parallel exchange sizes are read on the host)",
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
-                    "d2h_bytes_per_step": nbytes},
+                    "d2h_bytes_per_step": nbytes, "ms_per_step": e2e_ms / args.steps,
+                    "copies": "pinned host <-> device on two copy streams, overlapped with "
+                              "the neighbouring steps' compute (two device slots)",
+                    "output_matches_device": e2e_ok},
             "gpu_launches": launches,
             "clocks": clocks,
         }

@@ -6,7 +6,7 @@
 
 #include <cstdint>
 
-#include "../../include/moe_b200.h"
+#include "moe_b200.h"
 #include "grouped_gemm.cuh"
 #include "moe_internal.h"
 
@@ -242,13 +242,13 @@ Built build_up(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_
   b.g.d_m_base = moe::BASE_TOK;
   b.g.d = out;
   b.g.ldd = ld_out;
+  b.g.d_rows = rows;
   b.epi = moe::EPI_STORE;
   if (activation == MOE_ACT_RELU_SQUARED) {
     b.epi = moe::EPI_RELU2;
-    // without a pre_act buffer the relu output is written to `out` first and
-    // then overwritten by its square (same element, same thread)
-    b.g.aux = pre_act ? pre_act : out;
+    b.g.aux = pre_act;  // may be null: only relu(acc)^2 is stored
     b.g.ld_aux = ld_out;
+    b.g.aux_rows = rows;
   }
   b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
                       pick_bn(tile_n, 0), 0};
@@ -272,6 +272,7 @@ Built build_down(const void* inter, int64_t rows, int64_t ld_inter, const void* 
   b.g.d_m_base = moe::BASE_TOK;
   b.g.d = out;
   b.g.ldd = ld_out;
+  b.g.d_rows = rows;
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
                       pick_bn(tile_n, hidden), 0};
@@ -295,6 +296,7 @@ Built build_up_dx(const void* grad_act, int64_t rows, int64_t ld_ga, const void*
   b.g.d_m_base = moe::BASE_TOK;
   b.g.d = grad_x;
   b.g.ldd = ld_gx;
+  b.g.d_rows = rows;
   b.epi = moe::EPI_STORE;
   // B = w1 read K-major: rows are the hidden (N) index, columns the width (K)
   b.op = GemmOperands{grad_act, rows, ld_ga, ld_ga, 0, w1, hidden, total_width, total_width, 0,
@@ -318,6 +320,7 @@ Built build_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_ac
   b.g.d_n_base = moe::BASE_WOFF;
   b.g.d = grad_w1;
   b.g.ldd = total_width;
+  b.g.d_rows = hidden;
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{x, rows, hidden, ld_x, 1, grad_act, rows, ld_ga, ld_ga, 1,
                       pick_bn(tile_n, 0), 0};
@@ -342,8 +345,10 @@ Built build_down_dinter(const void* grad_y, int64_t rows, int64_t ld_gy, const v
   b.g.d_m_base = moe::BASE_TOK;
   b.g.d = out;
   b.g.ldd = ld_out;
+  b.g.d_rows = rows;
   b.g.aux = const_cast<void*>(pre_act);
   b.g.ld_aux = ld_pre;
+  b.g.aux_rows = rows;
   b.epi = pre_act ? moe::EPI_DACT : moe::EPI_STORE;
   // B = w2 read K-major: rows are the width (N) index, columns the hidden (K)
   b.op = GemmOperands{grad_y, rows, hidden, ld_gy, 0, w2, total_width, hidden, hidden, 0,
@@ -367,6 +372,7 @@ Built build_down_dw(const void* inter, int64_t rows, int64_t ld_inter, const voi
   b.g.d_m_base = moe::BASE_WOFF;
   b.g.d = grad_w2;
   b.g.ldd = hidden;
+  b.g.d_rows = total_width;
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_gy, 1,
                       pick_bn(tile_n, hidden), 0};

@@ -32,32 +32,37 @@ constexpr int BN_MAX = 256;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-block
-constexpr int kRingBytes = 192 * 1024;   // smem ring for the A/B stages
-constexpr int kEpiBytes = 4 * 32 * 128;  // per epilogue warp: 32 rows x 128 bytes
+constexpr int kSmemMax = 227 * 1024;     // dynamic shared memory per CTA on sm_100
+constexpr int kEpiBytes = 4 * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
-constexpr int kSmemBytes = 1024 + kRingBytes + kEpiBytes + 256;
+constexpr int kBarBytes = 256;            // mbarriers, TMEM address, abort flag
 
 struct Problem {
   GroupedGemmDesc g;
   int a_mn, b_mn, epi, bn;
+  int d_tma;  // tmD is valid: full slabs leave through TMA stores
 };
 
 struct MultiParams {
   CUtensorMap tmA[kMaxProblems];
   CUtensorMap tmB[kMaxProblems];
+  CUtensorMap tmD[kMaxProblems];  // epilogue output, 32-row x 128-byte boxes
+  CUtensorMap tmX[kMaxProblems];  // epilogue aux (pre-activation), same boxes
   Problem pr[kMaxProblems];
   int nprob;
   int stages;       // stages in the ring (depends on the largest N tile)
   int stage_bytes;  // A tile + largest B tile
+  int smem_bytes;   // dynamic shared memory of the launch
 };
 
 // Per (problem, expert) slot: tile prefix, extents and the two offsets every
-// coordinate base is made of (token offset, weight offset).
+// coordinate base is made of (token offset, weight offset).  Lives in dynamic
+// shared memory behind the barriers, sized for the launch's slot count.
 struct Table {
-  int prefix[kMaxProblems * kMaxGroups + 1];
-  int M[kMaxProblems * kMaxGroups], N[kMaxProblems * kMaxGroups], K[kMaxProblems * kMaxGroups];
-  int tok[kMaxProblems * kMaxGroups], wof[kMaxProblems * kMaxGroups];
+  int* prefix;  // [nge + 1]
+  int *M, *N, *K, *tok, *wof;  // [nge] each
 };
+__host__ __device__ constexpr int table_bytes(int nge) { return (6 * nge + 1) * 4; }
 
 __device__ __forceinline__ int slot_base(int src, const Table& tb, int slot) {
   if (src == BASE_TOK) return tb.tok[slot];
@@ -270,23 +275,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int S = P.stages;
   const int SB = P.stage_bytes;
-  uint8_t* ring = smem;               // stage s: A at s*SB, B at s*SB + kABytes
-  uint8_t* sEpi = smem + kRingBytes;  // epilogue staging, 4 KB per warp
+  uint8_t* ring = smem;                // stage s: A at s*SB, B at s*SB + kABytes
+  uint8_t* sEpi = smem + S * SB;       // epilogue staging, 8 KB per warp
   uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   uint64_t* acc_full = bars + 2 * kMaxStages;
   uint64_t* acc_empty = bars + 2 * kMaxStages + 2;
   uint64_t* drain = bars + 2 * kMaxStages + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 5);
-
-  __shared__ Table tb;
-  __shared__ int abort_flag;
+  uint64_t* epi_ld = bars + 2 * kMaxStages + 5;  // [4 warps][2 slabs]: aux tile loads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
+  int& abort_flag = *reinterpret_cast<int*>(bars + 2 * kMaxStages + 14);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // (problem, expert) slots: problem 0's experts, then problem 1's
   const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
+  Table tb;
+  tb.prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);
+  tb.M = tb.prefix + nge + 1;
+  tb.N = tb.M + nge;
+  tb.K = tb.N + nge;
+  tb.tok = tb.K + nge;
+  tb.wof = tb.tok + nge;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -299,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&epi_ld[i], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -307,6 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&P.tmA[p]);
       tma_prefetch_desc(&P.tmB[p]);
     }
+  }
+  if (warp >= 2 && lane == 0 && warp - 2 < P.nprob) {
+    if (P.pr[warp - 2].d_tma) tma_prefetch_desc(&P.tmD[warp - 2]);
+    if (P.pr[warp - 2].epi == EPI_DACT) tma_prefetch_desc(&P.tmX[warp - 2]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -432,56 +448,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Results are
-    // produced one 128-byte-wide slab (64 bf16 / 32 fp32 columns) at a time: every lane converts its own row
-    // into a 32 x 128 B staging tile (16-byte chunks XOR-swizzled by row, so
-    // the row-per-lane writes and the row-major reads are bank-conflict free),
-    // then the warp stores the slab row-major, four full 128-byte rows per
-    // instruction.
+    // Each warp owns 32 accumulator rows (its TMEM lane quarter) and produces
+    // them one slab at a time: 32 rows x 128 bytes (64 bf16 / 32 fp32 columns).
+    // Every lane converts its own row into a shared staging slab laid out in
+    // the TMA 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)), then
+    // one lane stores the slab with a TMA tensor store and the warp moves on;
+    // two staging slabs per warp alternate, so a slab is rewritten only after
+    // its previous store has finished reading it.  Slabs that straddle an
+    // expert's last row or column are stored by the lanes instead (row-major,
+    // four 128-byte rows per instruction), never past the expert's extent.
+    // The relu^2-derivative epilogue fetches its pre-activation slab by TMA
+    // into the staging slab one slab ahead and computes in place.
     constexpr int EPC = Elem<T>::EPC;  // elements per 16-byte chunk
-    constexpr int SLAB = 8 * EPC;      // columns per 128-byte staging row
+    constexpr int SLAB = 8 * EPC;      // columns per slab
     const int q = warp & 3;
-    uint8_t* stg = sEpi + q * 4096;
+    uint8_t* stg_base = sEpi + q * 8192;
+    uint64_t* ldb = epi_ld + q * 2;
+    uint32_t ld_phase = 0;  // bit i: parity of the next wait on ldb[i]
+    int nbuf = 0;           // staging slab the next write goes to
     int buf = 0;
     uint32_t acc_phase = 0;
     const int rsub = lane >> 3;  // row within a 4-row group for the row-major phase
     const int csub = lane & 7;   // 16-byte chunk within a 128-byte row
-    auto stg_chunk = [&](int row, int chunk) -> uint4* {
+    auto chunk_at = [&](uint8_t* stg, int row, int chunk) -> uint4* {
       return reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4));
     };
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const Tile tl = decode_tile(tb, P, nge, t);
       const Problem& pr = P.pr[tl.p];
       const GroupedGemmDesc& g = pr.g;
       const int slot = tl.slot;
       const int M = tb.M[slot], N = tb.N[slot], K = tb.K[slot];
       const int epi = pr.epi;
+      const bool dact = epi == EPI_DACT;
+      const bool tma_out = pr.d_tma != 0;
+      const CUtensorMap* tmD = &P.tmD[tl.p];
+      const CUtensorMap* tmX = &P.tmX[tl.p];
       T* D = reinterpret_cast<T*>(g.d);
       T* AUX = reinterpret_cast<T*>(g.aux);
-      if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag)) break;
-      tc_fence_after();
       const int rbase = tl.m0 + q * 32;        // group row of this warp's first row
       const int rows_ok = min(32, M - rbase);  // may be <= 0
       const long long grow0 = static_cast<long long>(slot_base(g.d_m_base, tb, slot)) + rbase;
       const int gcol0 = slot_base(g.d_n_base, tb, slot) + tl.n0;
       const int ncols = min(pr.bn, N - tl.n0);
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                             static_cast<uint32_t>(buf * BN_MAX);
-      // row-major store of the staged slab (rows beyond the expert and columns
-      // beyond its width are skipped); all shared loads first, then the stores
-      auto store_slab = [&](T* dst, long long ld, int s, int cvalid) {
-        uint4 sv[8];
-#pragma unroll
-        for (int it = 0; it < 8; ++it) sv[it] = *stg_chunk(it * 4 + rsub, csub);
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int row = it * 4 + rsub;
-          if (row < rows_ok && csub * EPC < cvalid)
-            *reinterpret_cast<uint4*>(dst + (grow0 + row) * ld + gcol0 + s + csub * EPC) = sv[it];
+      // fetch an aux (pre-activation) slab into staging slab `b` (lane 0)
+      auto fetch_aux = [&](int b, int s) {
+        fence_proxy_async_smem();  // the lanes' reads of the slab precede the load
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ldb[b], 32 * 128);
+          tma_load_2d(stg_base + b * 4096, tmX, &ldb[b], gcol0 + s, static_cast<int>(grow0));
         }
       };
+      if (dact) {
+        // every earlier store has finished reading both staging slabs
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+        nbuf = 0;
+        if (rows_ok > 0) fetch_aux(0, 0);  // overlaps the wait for the accumulator
+      }
+      if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(buf * BN_MAX);
+      // store the staged slab: TMA for full slabs, lanes for ragged ones
+      auto put = [&](uint8_t* stg, const CUtensorMap* tm, T* dst, long long ld, int s,
+                     int cvalid) {
+        if (tma_out && cvalid == SLAB && rows_ok == 32) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tm, stg, gcol0 + s, static_cast<int>(grow0));
+            bulk_commit_group();
+          }
+        } else {
+          __syncwarp();
+          uint4 sv[8];
+#pragma unroll
+          for (int it = 0; it < 8; ++it) sv[it] = *chunk_at(stg, it * 4 + rsub, csub);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int row = it * 4 + rsub;
+            if (row < rows_ok && csub * EPC < cvalid)
+              *reinterpret_cast<uint4*>(dst + (grow0 + row) * ld + gcol0 + s + csub * EPC) =
+                  sv[it];
+          }
+          __syncwarp();
+        }
+      };
+      // the next staging slab, once its previous TMA store has read it
+      auto next_stage = [&]() -> uint8_t* {
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* p = stg_base + nbuf * 4096;
+        nbuf ^= 1;
+        return p;
+      };
 #pragma unroll 1
-      for (int s = 0; s < ncols; s += SLAB) {
+      for (int s = 0; s < ncols && rows_ok > 0; s += SLAB) {
         const int cvalid = min(SLAB, ncols - s);
         float v[SLAB];
         if (K > 0) {
@@ -492,56 +557,51 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < SLAB; ++i) v[i] = 0.f;
         }
-        if (epi == EPI_DACT) {
-          // stage pre (row-major, coalesced; all eight loads in flight first)
-          uint4 pv[8];
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int row = it * 4 + rsub;
-            pv[it] = make_uint4(0, 0, 0, 0);
-            if (row < rows_ok && csub * EPC < cvalid)
-              pv[it] = __ldg(reinterpret_cast<const uint4*>(AUX + (grow0 + row) * g.ld_aux +
-                                                            gcol0 + s + csub * EPC));
+        if (dact) {
+          const int b = (s / SLAB) & 1;
+          uint8_t* stg = stg_base + b * 4096;
+          if (!mbar_wait(&ldb[b], (ld_phase >> b) & 1, &abort_flag)) {
+            ok = false;
+            break;
           }
-#pragma unroll
-          for (int it = 0; it < 8; ++it) *stg_chunk(it * 4 + rsub, csub) = pv[it];
-          __syncwarp();
+          ld_phase ^= 1u << b;
+          if (s + SLAB < ncols) {
+            // prefetch the next aux slab into the other staging slab (its
+            // previous store, if any, must have finished reading it)
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            fetch_aux(b ^ 1, s + SLAB);
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float pr_[EPC], o[EPC];
-            unpack_chunk<T>(*stg_chunk(lane, j), pr_);
+            unpack_chunk<T>(*chunk_at(stg, lane, j), pr_);
 #pragma unroll
             for (int i = 0; i < EPC; ++i) {
               const float gi = Cvt<T>::round(v[j * EPC + i]);
               o[i] = pr_[i] > 0.f ? gi * 2.0f * pr_[i] : 0.f;
             }
-            *stg_chunk(lane, j) = pack_chunk<T>(o);
+            *chunk_at(stg, lane, j) = pack_chunk<T>(o);
           }
-          __syncwarp();
-          store_slab(D, g.ldd, s, cvalid);
-          __syncwarp();
+          put(stg, tmD, D, g.ldd, s, cvalid);
+          nbuf = b ^ 1;  // the other slab is the older one now
         } else {
           if (epi == EPI_RELU2) {
 #pragma unroll
             for (int i = 0; i < SLAB; ++i) v[i] = fmaxf(v[i], 0.f);
-          }
+            if (AUX != nullptr) {
+              uint8_t* stg = next_stage();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) *stg_chunk(lane, j) = pack_chunk<T>(&v[j * EPC]);
-          __syncwarp();
-          if (epi == EPI_RELU2) {
-            store_slab(AUX, g.ld_aux, s, cvalid);  // pre = relu(acc)
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float sq[EPC];
-#pragma unroll
-              for (int i = 0; i < EPC; ++i) sq[i] = v[j * EPC + i] * v[j * EPC + i];
-              *stg_chunk(lane, j) = pack_chunk<T>(sq);
+              for (int j = 0; j < 8; ++j) *chunk_at(stg, lane, j) = pack_chunk<T>(&v[j * EPC]);
+              put(stg, tmX, AUX, g.ld_aux, s, cvalid);  // pre = relu(acc)
             }
-            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < SLAB; ++i) v[i] = v[i] * v[i];
           }
-          store_slab(D, g.ldd, s, cvalid);
-          __syncwarp();
+          uint8_t* stg = next_stage();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) *chunk_at(stg, lane, j) = pack_chunk<T>(&v[j * EPC]);
+          put(stg, tmD, D, g.ldd, s, cvalid);
         }
       }
       tc_fence_before();
@@ -550,6 +610,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
+    // stores must be complete (not only done reading smem) before exit
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   }
 
   __syncthreads();
@@ -612,7 +675,7 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax) !=
             cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
             cudaSuccess)
@@ -627,7 +690,7 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = P.smem_bytes;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -680,6 +743,20 @@ int num_sms() {
   return n;
 }
 
+// Ring stages and dynamic shared memory of a launch: the ring takes what the
+// alignment pad, epilogue staging, barriers and the slot table leave.
+static bool plan_smem(MultiParams& P, int bn_max) {
+  const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
+  P.stage_bytes = kABytes + bn_max * 128;
+  const int fixed = 1024 + kEpiBytes + kBarBytes + table_bytes(nge);
+  int stages = (kSmemMax - fixed) / P.stage_bytes;
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) return false;
+  P.stages = stages;
+  P.smem_bytes = fixed + stages * P.stage_bytes;
+  return true;
+}
+
 template <typename T>
 int dispatch(int used, int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
   if (used == 1) return launch_single<T>(c0, P, grid, st);
@@ -718,6 +795,19 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     if (op.b_mn) s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bke, true);
     else s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bn, false);
     if (s) return s;
+    // epilogue maps: 32-row x 128-byte boxes in the staging-slab swizzle
+    {
+      const int sd = g.d_rows > 0
+                         ? make_tmap(&P.tmD[used], g.d, dtype, g.ldd, g.d_rows, g.ldd, bke, 32, false)
+                         : kStatusBadArg;
+      int sx = kStatusOk;
+      if (g.aux != nullptr && epis[i] != EPI_STORE)
+        sx = g.aux_rows > 0 ? make_tmap(&P.tmX[used], g.aux, dtype, g.ld_aux, g.aux_rows,
+                                        g.ld_aux, bke, 32, false)
+                            : kStatusBadArg;
+      if (epis[i] == EPI_DACT && sx != kStatusOk) return kStatusBadArg;
+      P.pr[used].d_tma = (sd == kStatusOk && sx == kStatusOk) ? 1 : 0;
+    }
     P.pr[used].g = g;
     P.pr[used].a_mn = op.a_mn;
     P.pr[used].b_mn = op.b_mn;
@@ -729,9 +819,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   }
   if (used == 0) return kStatusOk;
   P.nprob = used;
-  P.stage_bytes = kABytes + bn_max * 128;
-  P.stages = kRingBytes / P.stage_bytes;
-  if (P.stages > kMaxStages) P.stages = kMaxStages;
+  if (!plan_smem(P, bn_max)) return kStatusUnsupported;
   if (grid <= 0) grid = num_sms();
   const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn);
   const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn) : c0;
@@ -743,9 +831,10 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     Q.nprob = 1;
     Q.tmA[0] = P.tmA[i];
     Q.tmB[0] = P.tmB[i];
+    Q.tmD[0] = P.tmD[i];
+    Q.tmX[0] = P.tmX[i];
     Q.pr[0] = P.pr[i];
-    Q.stage_bytes = kABytes + P.pr[i].bn * 128;
-    Q.stages = kRingBytes / Q.stage_bytes > kMaxStages ? kMaxStages : kRingBytes / Q.stage_bytes;
+    if (!plan_smem(Q, P.pr[i].bn)) return kStatusUnsupported;
     const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn);
     rc = dispatch_dtype(dtype, 1, ci, ci, Q, grid, st);
     if (rc != kStatusOk) return rc;

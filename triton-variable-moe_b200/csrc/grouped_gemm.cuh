@@ -51,8 +51,10 @@ struct GroupedGemmDesc {
   // epilogue
   void* d;
   long long ldd;
+  long long d_rows;  // rows of the D allocation (its tensor map extent)
   void* aux;
   long long ld_aux;
+  long long aux_rows;  // rows of the aux allocation
   int* status;  // device status word: set non-zero when a wait gave up
 };
 

@@ -26,6 +26,7 @@ namespace {
 
 constexpr int kMaxE = 256;
 constexpr int kWarpsPerBlock = 8;
+constexpr int kBatch = 8;  // warp-steps of ids loaded together per lane
 
 struct RouteOut {
   int32_t* bin_ids;
@@ -47,16 +48,6 @@ __device__ __forceinline__ int rounded_count(int n, int bs, int mode) {
   return ((n + bs / 2) / bs) * bs;
 }
 
-template <typename S>
-__device__ __forceinline__ int load_expert(const S* sel, long long i, int E, int* status) {
-  const long long v = static_cast<long long>(sel[i]);
-  if (v < 0 || v >= E) {
-    if (status) atomicExch(status, kStatusBadExpert);
-    return -1;
-  }
-  return static_cast<int>(v);
-}
-
 // ---- phase 1: per-unit histograms -------------------------------------------
 template <typename S>
 __global__ void route_count_kernel(const S* __restrict__ sel, long long A, int E, long long U,
@@ -70,9 +61,26 @@ __global__ void route_count_kernel(const S* __restrict__ sel, long long A, int E
   __syncwarp();
   if (unit < units) {
     const long long beg = unit * U, end = min(A, beg + U);
-    for (long long i = beg + lane; i < end; i += 32) {
-      const int e = load_expert(sel, i, E, status);
-      if (e >= 0) atomicAdd(&hist[w][e], 1);
+    // kBatch independent loads in flight per lane before the shared atomics
+    for (long long i0 = beg + lane; i0 < end; i0 += 32LL * kBatch) {
+      S v[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const long long i = i0 + 32LL * j;
+        v[j] = i < end ? sel[i] : S(0);
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const long long i = i0 + 32LL * j;
+        if (i < end) {
+          const long long e = static_cast<long long>(v[j]);
+          if (e < 0 || e >= E) {
+            if (status) atomicExch(status, kStatusBadExpert);
+          } else {
+            atomicAdd(&hist[w][e], 1);
+          }
+        }
+      }
     }
     __syncwarp();
     for (int e = lane; e < E; e += 32) ws[unit * E + e] = hist[w][e];
@@ -141,6 +149,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     const int e = e0 + g;
     int tot = 0, bef = 0;
     if (g < groups && e < E) {
+#pragma unroll 4
       for (long long u = part; u < units; u += parts) {
         const int c = ws[u * E + e];
         tot += c;
@@ -216,10 +225,28 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   const long long unit = u0 + w;
   if (unit < units) {
     const long long beg = unit * U, end = min(A, beg + U);
+    int ev[kBatch];
     for (long long i0 = beg; i0 < end; i0 += 32) {
       const long long i = i0 + lane;
       const bool valid = i < end;
-      const int e = valid ? load_expert(sel, i, E, nullptr) : -1;
+      const int jb = static_cast<int>(((i0 - beg) >> 5) % kBatch);
+      if (jb == 0) {
+        // the next kBatch warp-steps' ids, all loads in flight together
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const long long ij = i + 32LL * j;
+          ev[j] = -1;
+          if (ij < end) {
+            const long long v = static_cast<long long>(sel[ij]);
+            ev[j] = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+          }
+        }
+      }
+      int e = -1;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (j == jb) e = ev[j];
+      if (!valid) e = -1;
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       const int rank_in = __popc(peers & ((1u << lane) - 1u));
       if (e >= 0) {

@@ -40,31 +40,36 @@ def _count(n: int = 1) -> None:
 
 
 _kernel_events: list | None = None
+_events_external = False
 
 
 @contextmanager
-def record_kernel_events():
-    """Within the block, every grouped GEMM launch is bracketed by CUDA events
-    on its launch stream; yields the list of (name, start, end) events."""
-    global _kernel_events
+def record_kernel_events(external: bool = False):
+    """Within the block, every launch of ours is bracketed by CUDA events on its
+    launch stream; yields the list of (name, start, end) events.  With
+    external=True the events are recorded as event-record nodes when the block
+    runs under CUDA-graph capture, so replays of the graph time each kernel."""
+    global _kernel_events, _events_external
     prev, _kernel_events = _kernel_events, []
+    prev_ext, _events_external = _events_external, external
     try:
         yield _kernel_events
     finally:
         _kernel_events = prev
+        _events_external = prev_ext
 
 
 def _ev_begin():
     if _kernel_events is None:
         return None
-    e = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True, external=_events_external)
     e.record()
     return e
 
 
 def _ev_end(start, name: str) -> None:
     if start is not None:
-        e = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True, external=_events_external)
         e.record()
         _kernel_events.append((name, start, e))
 
