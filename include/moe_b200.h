@@ -46,6 +46,8 @@ extern "C" {
 #define MOE_DTYPE_F16 1
 #define MOE_DTYPE_F32 2
 
+#define MOE_TILE_PAIR 0x200 /* tile_n flag: 256-row tiles on SM pairs */
+
 #define MOE_ACT_NONE 0
 #define MOE_ACT_RELU_SQUARED 1
 
@@ -202,7 +204,9 @@ MOE_API int moe_relu_squared_grad(const void* grad_out, const void* pre_act, int
  *   hidden                hidden size H; w1 is [H, total_width], w2 is
  *                         [total_width, H], both contiguous
  *   rows                  rows of the token-space operands (allocation size)
- *   tile_n                128 or 256 (0 = choose)
+ *   tile_n                N tile 128 or 256 (0 = choose); OR MOE_TILE_PAIR for
+ *                         256-row tiles computed by SM pairs (2-CTA clusters,
+ *                         cta_group::2 MMAs) instead of 128-row tiles
  * Every expert width and every expert row count used as a reduction length
  * must be a multiple of 16; H must be a multiple of 16.
  */

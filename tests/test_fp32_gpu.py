@@ -37,7 +37,7 @@ FP32_CASES = CASES + [([48, 16, 112], [33, 17, 70], 80, 16)]  # k tails of 16 in
 
 
 @pytest.mark.parametrize("case", FP32_CASES, ids=[f"c{i}" for i in range(len(FP32_CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", [128, 256, 128 | 0x200, 256 | 0x200])
 def test_fp32_forward(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -63,7 +63,8 @@ def test_fp32_forward(case, tile_n, device):
 
 
 @pytest.mark.parametrize("case", FP32_CASES, ids=[f"c{i}" for i in range(len(FP32_CASES))])
-def test_fp32_backward(case, device):
+@pytest.mark.parametrize("pair", [0, 0x200])
+def test_fp32_backward(case, pair, device):
     from moe_b200.kernels import _ops
 
     widths, counts, H, bs = case
@@ -72,11 +73,11 @@ def test_fp32_backward(case, device):
     dact = torch.zeros(m["rows"], m["maxw"], dtype=F32, device=device)
     gw2 = torch.full((m["TW"], H), 7.0, dtype=F32, device=device)
     _ops.gemm_down_backward(t["gy"], t["ga"], t["w2"], *args, dact, gw2, pre_act=t["pre"],
-                            tile_n_width=128, tile_n_hidden=256)
+                            tile_n_width=128 | pair, tile_n_hidden=256 | pair)
     gx = torch.zeros(m["rows"], H, dtype=F32, device=device)
     gw1 = torch.full((H, m["TW"]), 7.0, dtype=F32, device=device)
-    _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1, tile_n_width=128,
-                          tile_n_hidden=256)
+    _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1, tile_n_width=128 | pair,
+                          tile_n_hidden=256 | pair)
     torch.cuda.synchronize()
     for e in range(m["E"]):
         r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]

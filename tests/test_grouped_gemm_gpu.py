@@ -15,6 +15,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 RTOL, ATOL = 2e-2, 1e-2
+PAIR = 0x200  # tile_n flag (MOE_TILE_PAIR): 256-row tiles on 2-CTA clusters
+TILES = [128, 256, 128 | PAIR, 256 | PAIR]
 
 
 def assert_close(a, b, what):
@@ -76,7 +78,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", TILES)
 def test_up_forward(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -115,7 +117,7 @@ def test_up_forward_no_activation(case, device):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", TILES)
 def test_down_forward(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -133,14 +135,15 @@ def test_down_forward(case, tile_n, device):
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
 @pytest.mark.parametrize("fused", [False, True])
-def test_down_dinter(case, fused, device):
+@pytest.mark.parametrize("tile_n", [0, 128 | PAIR])
+def test_down_dinter(case, fused, tile_n, device):
     from moe_b200.kernels import _ops
 
     widths, counts, H, bs = case
     t, m = make_problem(widths, counts, H, bs, device=device, seed=3)
     out = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
     _ops.gemm_down_dinter(t["gy"], t["w2"], m["tok_off"], m["w_off"], m["tpe"], m["E"], out,
-                          pre_act=t["pre"] if fused else None)
+                          pre_act=t["pre"] if fused else None, tile_n=tile_n)
     torch.cuda.synchronize()
     for e in range(m["E"]):
         r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]
@@ -154,7 +157,7 @@ def test_down_dinter(case, fused, device):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", TILES)
 def test_up_dx(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -171,7 +174,7 @@ def test_up_dx(case, tile_n, device):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", TILES)
 def test_up_dw(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -187,7 +190,7 @@ def test_up_dw(case, tile_n, device):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_n", TILES)
 def test_down_dw(case, tile_n, device):
     from moe_b200.kernels import _ops
 
@@ -216,9 +219,10 @@ def test_fp16_up(device):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-def test_fused_backward_launches(case, device):
+@pytest.mark.parametrize("pair", [0, PAIR])
+def test_fused_backward_launches(case, pair, device):
     """The two-problem launches (dIntermediate+dW2, dX+dW1) give the same
-    results as the single-problem launches."""
+    results as the single-problem launches (128-row or paired 256-row tiles)."""
     from moe_b200.kernels import _ops
 
     widths, counts, H, bs = case
@@ -227,22 +231,24 @@ def test_fused_backward_launches(case, device):
     dact = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
     gw2 = torch.full((m["TW"], H), 7.0, dtype=torch.bfloat16, device=device)
     _ops.gemm_down_backward(t["gy"], t["ga"], t["w2"], *args, dact, gw2, pre_act=t["pre"],
-                            tile_n_width=128, tile_n_hidden=256)
+                            tile_n_width=128 | pair, tile_n_hidden=256 | pair)
     dact_ref = torch.zeros_like(dact)
-    _ops.gemm_down_dinter(t["gy"], t["w2"], *args, dact_ref, pre_act=t["pre"])
+    _ops.gemm_down_dinter(t["gy"], t["w2"], *args, dact_ref, pre_act=t["pre"], tile_n=128 | pair)
     gw2_ref = torch.zeros_like(gw2)
-    _ops.gemm_down_dw(t["ga"], t["gy"], m["tok_off"], m["w_off"], m["E"], gw2_ref, tile_n=256)
+    _ops.gemm_down_dw(t["ga"], t["gy"], m["tok_off"], m["w_off"], m["E"], gw2_ref,
+                      tile_n=256 | pair)
     torch.cuda.synchronize()
     assert torch.equal(dact, dact_ref)
     assert torch.equal(gw2, gw2_ref)
     gx = torch.zeros(m["rows"], H, dtype=torch.bfloat16, device=device)
     gw1 = torch.full((H, m["TW"]), 7.0, dtype=torch.bfloat16, device=device)
-    _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1, tile_n_width=128,
-                          tile_n_hidden=256)
+    _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1, tile_n_width=128 | pair,
+                          tile_n_hidden=256 | pair)
     gx_ref = torch.zeros_like(gx)
-    _ops.gemm_up_dx(t["ga"], t["w1"], *args, gx_ref, tile_n=256)
+    _ops.gemm_up_dx(t["ga"], t["w1"], *args, gx_ref, tile_n=256 | pair)
     gw1_ref = torch.zeros_like(gw1)
-    _ops.gemm_up_dw(t["x"], t["ga"], m["tok_off"], m["w_off"], m["E"], gw1_ref, tile_n=128)
+    _ops.gemm_up_dw(t["x"], t["ga"], m["tok_off"], m["w_off"], m["E"], gw1_ref,
+                    tile_n=128 | pair)
     torch.cuda.synchronize()
     assert torch.equal(gx, gx_ref)
     assert torch.equal(gw1, gw1_ref)

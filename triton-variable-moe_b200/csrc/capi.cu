@@ -56,9 +56,12 @@ bool gemm_dtype_ok(int dtype) {
 }
 
 int pick_bn(int tile_n, long long n_hint) {
-  if (tile_n == 128 || tile_n == 256) return tile_n;
+  const int t = tile_n & ~MOE_TILE_PAIR;
+  if (t == 128 || t == 256) return t;
   return (n_hint > 0 && n_hint % 256 == 0) ? 256 : 128;
 }
+// 2: 256-row tiles on 2-CTA clusters; 1: 128-row tiles on single CTAs.
+int pick_pair(int tile_n) { return (tile_n & MOE_TILE_PAIR) ? 2 : 1; }
 
 GroupedGemmDesc base_desc(const int32_t* tok_off, const int32_t* tok_cnt, const int32_t* w_off,
                           int E, long long hidden, int* status) {
@@ -252,6 +255,7 @@ Built build_up(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_
   }
   b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
                       pick_bn(tile_n, 0), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 
@@ -276,6 +280,7 @@ Built build_down(const void* inter, int64_t rows, int64_t ld_inter, const void* 
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
                       pick_bn(tile_n, hidden), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 
@@ -301,6 +306,7 @@ Built build_up_dx(const void* grad_act, int64_t rows, int64_t ld_ga, const void*
   // B = w1 read K-major: rows are the hidden (N) index, columns the width (K)
   b.op = GemmOperands{grad_act, rows, ld_ga, ld_ga, 0, w1, hidden, total_width, total_width, 0,
                       pick_bn(tile_n, hidden), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 
@@ -324,6 +330,7 @@ Built build_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_ac
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{x, rows, hidden, ld_x, 1, grad_act, rows, ld_ga, ld_ga, 1,
                       pick_bn(tile_n, 0), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 
@@ -353,6 +360,7 @@ Built build_down_dinter(const void* grad_y, int64_t rows, int64_t ld_gy, const v
   // B = w2 read K-major: rows are the width (N) index, columns the hidden (K)
   b.op = GemmOperands{grad_y, rows, hidden, ld_gy, 0, w2, total_width, hidden, hidden, 0,
                       pick_bn(tile_n, 0), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 
@@ -376,6 +384,7 @@ Built build_down_dw(const void* inter, int64_t rows, int64_t ld_inter, const voi
   b.epi = moe::EPI_STORE;
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_gy, 1,
                       pick_bn(tile_n, hidden), 0};
+  b.op.pair = pick_pair(tile_n);
   return b;
 }
 

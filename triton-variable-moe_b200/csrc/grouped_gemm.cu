@@ -35,7 +35,7 @@ constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-bl
 constexpr int kSmemMax = 227 * 1024;     // dynamic shared memory per CTA on sm_100
 constexpr int kEpiBytes = 4 * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
-constexpr int kBarBytes = 256;            // mbarriers, TMEM address, abort flag
+constexpr int kBarBytes = 512;            // mbarriers, TMEM address, abort flag
 
 struct Problem {
   GroupedGemmDesc g;
@@ -162,6 +162,7 @@ struct Tile {
   int p, e, m0, n0, slot;
 };
 
+template <int BMT>
 __device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& P, int nge,
                                             int t) {
   int lo = 0, hi = nge - 1;  // last (problem, expert) slot with prefix <= t
@@ -177,7 +178,7 @@ __device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& 
   const int bn = P.pr[r.p].bn;
   const int local = t - tb.prefix[lo];
   const int ntn = (tb.N[lo] + bn - 1) / bn;
-  r.m0 = (local / ntn) * BM;
+  r.m0 = (local / ntn) * BMT;
   r.n0 = (local % ntn) * bn;
   return r;
 }
@@ -189,14 +190,16 @@ constexpr int cfg_of(int a_mn, int b_mn, int bn) { return a_mn | (b_mn << 1) | (
 // Producer side of one tile: stream its k-blocks into the smem ring.  A tile
 // is 128 rows (A) / NT rows (B) of one 128-byte swizzle row of K each; an
 // MN-major operand arrives as 128-byte-wide MN blocks, one box each.
-template <int CFG, typename T>
+// With a CTA pair (CG = 2) each CTA loads its own 128 rows of A and its half
+// (NT / 2 rows) of B; am / bn are already offset to this CTA's share.
+template <int CFG, typename T, int CG>
 __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint64_t* full,
                                              uint64_t* empty, volatile int* abort_flag,
                                              const void* tA, const void* tB, int nkb, int am,
                                              int ak, int bn, int bk, int& stage,
                                              uint32_t& phase) {
   constexpr bool A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
-  constexpr int NT = (CFG & 4) ? 256 : 128;
+  constexpr int NT = ((CFG & 4) ? 256 : 128) / CG;  // B rows this CTA loads
   constexpr int BKE = Elem<T>::BKE;
   constexpr uint32_t bytes = kABytes + NT * 128;
   for (int kb = 0; kb < nkb; ++kb) {
@@ -228,15 +231,19 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
 }
 
 // MMA side of one tile: issue its k-blocks into the TMEM accumulator.
-template <int CFG, typename T>
+// With a CTA pair (CG = 2) this runs on the even CTA only: a stage is used
+// once both CTAs' halves have landed (`peer_full` is arrived on by the odd
+// CTA's relay), one M = 256 MMA covers both halves, and the stage is released
+// in both CTAs.
+template <int CFG, typename T, int CG>
 __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t* full,
-                                         uint64_t* empty, volatile int* abort_flag,
-                                         uint32_t d_tmem, int K, int nkb, int& stage,
-                                         uint32_t& phase) {
+                                         uint64_t* peer_full, uint64_t* empty,
+                                         volatile int* abort_flag, uint32_t d_tmem, int K,
+                                         int nkb, int& stage, uint32_t& phase) {
   constexpr int A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = (CFG & 4) ? 256 : 128;
   constexpr int BKE = Elem<T>::BKE, UKE = Elem<T>::UKE;
-  constexpr uint32_t idesc = idesc_mma(BM, NT, A_MN, B_MN, Elem<T>::FMT);
+  constexpr uint32_t idesc = idesc_mma(BM * CG, NT, A_MN, B_MN, Elem<T>::FMT);
   // K-major: the next K step is 32 bytes further along the swizzled row.
   // MN-major: it is UKE rows (of 128 bytes) further; MN blocks are LBO apart.
   constexpr uint32_t a_step = A_MN ? UKE * 128u : 32u, a_lbo = A_MN ? BKE * 128u : 16u;
@@ -247,6 +254,8 @@ __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t*
   constexpr uint32_t b_sbo = (B_MN && kW) ? 512u : 1024u, b_lay = (B_MN && kW) ? 1u : 2u;
   for (int kb = 0; kb < nkb; ++kb) {
     if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
+    if constexpr (CG == 2)
+      if (!mbar_wait_cluster(&peer_full[stage], phase, abort_flag)) return false;
     tc_fence_after();
     const uint32_t a_addr = smem_u32(ring + stage * SB);
     const uint32_t b_addr = a_addr + kABytes;
@@ -255,10 +264,12 @@ __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t*
       const uint64_t ad = smem_desc_sw128(a_addr + kk * a_step, a_lbo, a_sbo, a_lay);
       const uint64_t bd = smem_desc_sw128(b_addr + kk * b_step, b_lbo, b_sbo, b_lay);
       const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-      if constexpr (sizeof(T) == 4) tc_mma_tf32(d_tmem, ad, bd, idesc, acc);
-      else tc_mma_f16(d_tmem, ad, bd, idesc, acc);
+      if constexpr (sizeof(T) == 4) tc_mma_tf32<CG>(d_tmem, ad, bd, idesc, acc);
+      else tc_mma_f16<CG>(d_tmem, ad, bd, idesc, acc);
     }
-    tc_commit(&empty[stage]);  // smem stage free once these MMAs retire
+    // smem stage free (in both CTAs of a pair) once these MMAs retire
+    if constexpr (CG == 2) tc_commit_pair(&empty[stage]);
+    else tc_commit(&empty[stage]);
     if (++stage == S) {
       stage = 0;
       phase ^= 1;
@@ -267,9 +278,13 @@ __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t*
   return true;
 }
 
-template <typename T, int CFG0, int CFG1>
+// CG = 2: launched as 2-CTA clusters; the pair computes 256-row tiles with
+// cta_group::2 MMAs issued by the even CTA, each CTA holding its 128 rows of
+// the accumulator and running its own producer and epilogue.
+template <typename T, int CFG0, int CFG1, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ MultiParams P) {
+  constexpr int BMT = BM * CG;  // tile rows
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -286,6 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* epi_ld = bars + 2 * kMaxStages + 5;  // [4 warps][2 slabs]: aux tile loads
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
   int& abort_flag = *reinterpret_cast<int*>(bars + 2 * kMaxStages + 14);
+  uint64_t* peer_full = bars + 2 * kMaxStages + 15;  // [stages], even CTA of a pair
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int unit = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int nunits = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -304,10 +323,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+      mbar_init(&peer_full[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[i], 4 * CG);  // one arrival per epilogue warp of the pair
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 8; ++i) mbar_init(&epi_ld[i], 1);
@@ -325,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (P.pr[warp - 2].epi == EPI_DACT) tma_prefetch_desc(&P.tmX[warp - 2]);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc<CG>(tmem_slot, kTmemCols);
+    tmem_relinquish<CG>();
     tc_fence_before();
   }
   // Everything above touched only this CTA's own resources; from here on the
@@ -361,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (base_value(g.d_n_base, e, g) % kAlign) != 0;
         if (bad && g.status != nullptr) atomicExch(g.status, kStatusBadArg);
         const int bn = P.pr[p].bn;
-        tiles = (!bad && M > 0 && N > 0) ? ((M + BM - 1) / BM) * ((N + bn - 1) / bn) : 0;
+        tiles = (!bad && M > 0 && N > 0) ? ((M + BMT - 1) / BMT) * ((N + bn - 1) / bn) : 0;
       }
       tb.M[s] = M;
       tb.N[s] = N;
@@ -382,6 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 31) tb.prefix[nge] = incl;
   }
   __syncthreads();
+  // a pair's barriers are initialised before either CTA signals the other's
+  if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
   // The next kernel may start its own prologue now; it waits for this grid's
   // completion before touching memory.
@@ -395,55 +417,89 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const Tile tl = decode_tile(tb, P, nge, t);
+      for (int t = unit; t < total && ok; t += nunits) {
+        const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const Problem& pr = P.pr[tl.p];
         const GroupedGemmDesc& g = pr.g;
         const int K = tb.K[tl.slot];
         const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
-        const int am = slot_base(g.a_m_base, tb, tl.slot) + tl.m0;
+        const int am = slot_base(g.a_m_base, tb, tl.slot) + tl.m0 + static_cast<int>(rank) * BM;
         const int ak = slot_base(g.a_k_base, tb, tl.slot);
-        const int bn = slot_base(g.b_n_base, tb, tl.slot) + tl.n0;
+        const int bn = slot_base(g.b_n_base, tb, tl.slot) + tl.n0 +
+                       static_cast<int>(rank) * (pr.bn / CG);
         const int bk = slot_base(g.b_k_base, tb, tl.slot);
         if (tl.p == 0)
-          ok = produce_tile<CFG0, T>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0], &P.tmB[0],
-                                  nkb, am, ak, bn, bk, stage, phase);
+          ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0],
+                                         &P.tmB[0], nkb, am, ak, bn, bk, stage, phase);
         else
-          ok = produce_tile<CFG1, T>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1], &P.tmB[1],
-                                  nkb, am, ak, bn, bk, stage, phase);
+          ok = produce_tile<CFG1, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1],
+                                         &P.tmB[1], nkb, am, ak, bn, bk, stage, phase);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const Tile tl = decode_tile(tb, P, nge, t);
+      for (int t = unit; t < total && ok; t += nunits) {
+        const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int K = tb.K[tl.slot];
         const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
-        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag)) break;
+        bool free_acc;
+        if constexpr (CG == 2) free_acc = mbar_wait_cluster(&acc_empty[buf], acc_phase ^ 1, &abort_flag);
+        else free_acc = mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag);
+        if (!free_acc) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN_MAX);
         if (tl.p == 0)
-          ok = mma_tile<CFG0, T>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
-                                   phase);
+          ok = mma_tile<CFG0, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, d_tmem,
+                                     K, nkb, stage, phase);
         else
-          ok = mma_tile<CFG1, T>(ring, SB, S, full, empty, &abort_flag, d_tmem, K, nkb, stage,
-                                   phase);
+          ok = mma_tile<CFG1, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, d_tmem,
+                                     K, nkb, stage, phase);
         if (!ok) break;
-        if (nkb > 0) tc_commit(&acc_full[buf]);
-        else mbar_arrive(&acc_full[buf]);
+        if constexpr (CG == 2) {
+          if (nkb > 0) {
+            tc_commit_pair(&acc_full[buf]);
+          } else {
+            mbar_arrive(&acc_full[buf]);
+            mbar_arrive_remote(&acc_full[buf], 1);
+          }
+        } else {
+          if (nkb > 0) tc_commit(&acc_full[buf]);
+          else mbar_arrive(&acc_full[buf]);
+        }
         buf ^= 1;
         if (buf == 0) acc_phase ^= 1;
       }
       // Make sure no MMA is still in flight before TMEM is released.
-      tc_commit(drain);
+      tc_commit<CG>(drain);
       mbar_wait(drain, 0, &abort_flag);
+    } else if (CG == 2 && lane == 0) {
+      // odd CTA of a pair: tell the even CTA's MMA issuer when each of this
+      // CTA's stages has landed
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = unit; t < total && ok; t += nunits) {
+        const Tile tl = decode_tile<BMT>(tb, P, nge, t);
+        const int nkb = (tb.K[tl.slot] + Elem<T>::BKE - 1) / Elem<T>::BKE;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_remote(&peer_full[stage], 0);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
     }
     __syncwarp();
   } else {
@@ -474,8 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4));
     };
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const Tile tl = decode_tile(tb, P, nge, t);
+    for (int t = unit; t < total && ok; t += nunits) {
+      const Tile tl = decode_tile<BMT>(tb, P, nge, t);
       const Problem& pr = P.pr[tl.p];
       const GroupedGemmDesc& g = pr.g;
       const int slot = tl.slot;
@@ -487,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const CUtensorMap* tmX = &P.tmX[tl.p];
       T* D = reinterpret_cast<T*>(g.d);
       T* AUX = reinterpret_cast<T*>(g.aux);
-      const int rbase = tl.m0 + q * 32;        // group row of this warp's first row
+      const int rbase = tl.m0 + static_cast<int>(rank) * BM + q * 32;  // this warp's first row
       const int rows_ok = min(32, M - rbase);  // may be <= 0
       const long long grow0 = static_cast<long long>(slot_base(g.d_m_base, tb, slot)) + rbase;
       const int gcol0 = slot_base(g.d_n_base, tb, slot) + tl.n0;
@@ -606,7 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&acc_empty[buf]);
+        else mbar_arrive_remote(&acc_empty[buf], 0);
+      }
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
@@ -616,9 +675,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
+  // neither CTA of a pair leaves (or frees TMEM) while the other may still
+  // use its shared memory or tensor memory
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc<CG>(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0 && abort_flag) {
     for (int p = 0; p < P.nprob; ++p)
@@ -668,65 +730,78 @@ int make_tmap(CUtensorMap* tm, const void* base, int dtype, long long inner, lon
   return r == CUDA_SUCCESS ? kStatusOk : kStatusBadArg;
 }
 
-template <typename T, int C0, int C1>
+template <typename T, int C0, int C1, int CG>
 int launch(const MultiParams& P, int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<T, C0, C1>;
-  static bool attr_set[64] = {};  // per device
+  auto kern = grouped_gemm_kernel<T, C0, C1, CG>;
+  static bool attr_set[64] = {};   // per device
+  static int max_pairs[64] = {};   // co-resident 2-CTA clusters, per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev < 0 || dev >= 64) return kStatusCuda;
+  // Programmatic dependent launch: this grid's prologue (barrier init, TMEM
+  // allocation, descriptor prefetch) overlaps the tail of the previous kernel.
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = CG;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = P.smem_bytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG == 2 ? 2 : 1;
+  if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax) !=
             cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
             cudaSuccess)
       return kStatusCuda;
+    if (CG == 2) {
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
+        return kStatusCuda;
+      max_pairs[dev] = n;
+    }
     attr_set[dev] = true;
   }
-  // Programmatic dependent launch: this grid's prologue (barrier init, TMEM
-  // allocation, descriptor prefetch) overlaps the tail of the previous kernel.
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
+  if (CG == 2) {
+    grid = (grid / 2) * 2;
+    if (grid > 2 * max_pairs[dev] || grid <= 0) grid = 2 * max_pairs[dev];
+  }
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = P.smem_bytes;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return kStatusCuda;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
 }
 
 // One problem: any of the 8 operand configurations.
-template <typename T, int C>
-int launch_single_cfg(const MultiParams& P, int grid, cudaStream_t st) {
-  return launch<T, C, C>(P, grid, st);
-}
-template <typename T>
+template <typename T, int CG>
 int launch_single(int c, const MultiParams& P, int grid, cudaStream_t st) {
   switch (c) {
-    case 0: return launch_single_cfg<T, 0>(P, grid, st);
-    case 1: return launch_single_cfg<T, 1>(P, grid, st);
-    case 2: return launch_single_cfg<T, 2>(P, grid, st);
-    case 3: return launch_single_cfg<T, 3>(P, grid, st);
-    case 4: return launch_single_cfg<T, 4>(P, grid, st);
-    case 5: return launch_single_cfg<T, 5>(P, grid, st);
-    case 6: return launch_single_cfg<T, 6>(P, grid, st);
-    default: return launch_single_cfg<T, 7>(P, grid, st);
+    case 0: return launch<T, 0, 0, CG>(P, grid, st);
+    case 1: return launch<T, 1, 1, CG>(P, grid, st);
+    case 2: return launch<T, 2, 2, CG>(P, grid, st);
+    case 3: return launch<T, 3, 3, CG>(P, grid, st);
+    case 4: return launch<T, 4, 4, CG>(P, grid, st);
+    case 5: return launch<T, 5, 5, CG>(P, grid, st);
+    case 6: return launch<T, 6, 6, CG>(P, grid, st);
+    default: return launch<T, 7, 7, CG>(P, grid, st);
   }
 }
 // Two problems: a K-major/K-major problem followed by an MN-major/MN-major one
 // (the backward pairs), any N tiles.  Returns kStatusUnsupported otherwise.
-template <typename T>
+template <typename T, int CG>
 int launch_pair(int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
   if ((c0 & 3) != 0 || (c1 & 3) != 3) return kStatusUnsupported;
   const int k = ((c0 >> 2) & 1) | (((c1 >> 2) & 1) << 1);
   switch (k) {
-    case 0: return launch<T, 0, 3>(P, grid, st);
-    case 1: return launch<T, 4, 3>(P, grid, st);
-    case 2: return launch<T, 0, 7>(P, grid, st);
-    default: return launch<T, 4, 7>(P, grid, st);
+    case 0: return launch<T, 0, 3, CG>(P, grid, st);
+    case 1: return launch<T, 4, 3, CG>(P, grid, st);
+    case 2: return launch<T, 0, 7, CG>(P, grid, st);
+    default: return launch<T, 4, 7, CG>(P, grid, st);
   }
 }
 
@@ -745,9 +820,9 @@ int num_sms() {
 
 // Ring stages and dynamic shared memory of a launch: the ring takes what the
 // alignment pad, epilogue staging, barriers and the slot table leave.
-static bool plan_smem(MultiParams& P, int bn_max) {
+static bool plan_smem(MultiParams& P, int bn_max, int cg) {
   const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
-  P.stage_bytes = kABytes + bn_max * 128;
+  P.stage_bytes = kABytes + bn_max / cg * 128;
   const int fixed = 1024 + kEpiBytes + kBarBytes + table_bytes(nge);
   int stages = (kSmemMax - fixed) / P.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
@@ -757,17 +832,22 @@ static bool plan_smem(MultiParams& P, int bn_max) {
   return true;
 }
 
-template <typename T>
+template <typename T, int CG>
 int dispatch(int used, int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
-  if (used == 1) return launch_single<T>(c0, P, grid, st);
-  return launch_pair<T>(c0, c1, P, grid, st);
+  if (used == 1) return launch_single<T, CG>(c0, P, grid, st);
+  return launch_pair<T, CG>(c0, c1, P, grid, st);
 }
 
-int dispatch_dtype(int dtype, int used, int c0, int c1, const MultiParams& P, int grid,
+int dispatch_dtype(int dtype, int cg, int used, int c0, int c1, const MultiParams& P, int grid,
                    cudaStream_t st) {
-  if (dtype == 2) return dispatch<float>(used, c0, c1, P, grid, st);
-  if (dtype == 1) return dispatch<__half>(used, c0, c1, P, grid, st);
-  return dispatch<__nv_bfloat16>(used, c0, c1, P, grid, st);
+  if (cg == 2) {
+    if (dtype == 2) return dispatch<float, 2>(used, c0, c1, P, grid, st);
+    if (dtype == 1) return dispatch<__half, 2>(used, c0, c1, P, grid, st);
+    return dispatch<__nv_bfloat16, 2>(used, c0, c1, P, grid, st);
+  }
+  if (dtype == 2) return dispatch<float, 1>(used, c0, c1, P, grid, st);
+  if (dtype == 1) return dispatch<__half, 1>(used, c0, c1, P, grid, st);
+  return dispatch<__nv_bfloat16, 1>(used, c0, c1, P, grid, st);
 }
 
 int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
@@ -776,6 +856,10 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   MultiParams P;
   memset(&P, 0, sizeof(P));
   int bn_max = 128, grid = 0, used = 0;
+  // CTA pairs (256-row tiles) only when every problem of the launch asks
+  int cg = 2;
+  for (int i = 0; i < n; ++i)
+    if (gs[i].E != 0 && ops[i].pair != 2) cg = 1;
   for (int i = 0; i < n; ++i) {
     const GemmOperands& op = ops[i];
     const GroupedGemmDesc& g = gs[i];
@@ -793,7 +877,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     else s = make_tmap(&P.tmA[used], op.a, dtype, op.a_cols, op.a_rows, op.lda, bke, BM, false);
     if (s) return s;
     if (op.b_mn) s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bke, true);
-    else s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bn, false);
+    else s = make_tmap(&P.tmB[used], op.b, dtype, op.b_cols, op.b_rows, op.ldb, bke, bn / cg, false);
     if (s) return s;
     // epilogue maps: 32-row x 128-byte boxes in the staging-slab swizzle
     {
@@ -819,11 +903,11 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   }
   if (used == 0) return kStatusOk;
   P.nprob = used;
-  if (!plan_smem(P, bn_max)) return kStatusUnsupported;
+  if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0) grid = num_sms();
   const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn);
   const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn) : c0;
-  int rc = dispatch_dtype(dtype, used, c0, c1, P, grid, st);
+  int rc = dispatch_dtype(dtype, cg, used, c0, c1, P, grid, st);
   if (rc != kStatusUnsupported) return rc;
   // no compiled pair for these configurations: one launch per problem
   for (int i = 0; i < used; ++i) {
@@ -834,9 +918,9 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     Q.tmD[0] = P.tmD[i];
     Q.tmX[0] = P.tmX[i];
     Q.pr[0] = P.pr[i];
-    if (!plan_smem(Q, P.pr[i].bn)) return kStatusUnsupported;
+    if (!plan_smem(Q, P.pr[i].bn, cg)) return kStatusUnsupported;
     const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn);
-    rc = dispatch_dtype(dtype, 1, ci, ci, Q, grid, st);
+    rc = dispatch_dtype(dtype, cg, 1, ci, ci, Q, grid, st);
     if (rc != kStatusOk) return rc;
   }
   return kStatusOk;

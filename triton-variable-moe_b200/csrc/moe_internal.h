@@ -29,6 +29,7 @@ struct GemmOperands {
   int b_mn;
   int bn;    // N tile: 128 or 256
   int grid;  // CTAs; 0 = one per SM
+  int pair;  // 2: 256-row tiles on 2-CTA clusters (cta_group::2); else 128-row tiles
 };
 
 int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, int dtype,

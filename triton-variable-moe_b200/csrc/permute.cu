@@ -89,9 +89,11 @@ constexpr int kVecPerLane = 4;  // 16-byte vectors in flight per lane per batch
 
 // out[r, :] = src row map[r] / div of x (times w[map[r]] when w != null);
 // rows whose map entry is negative are zero.  Rows at or beyond *rows_dev
-// (when given) are not touched.  One warp per row; each lane issues up to four
-// 16-byte loads before its stores, so a 1024-wide bf16 row is one round trip.
-template <typename T, bool VEC>
+// (when given) are not touched.  A warp copies R consecutive rows at a time:
+// lanes fetch the R map entries (and weights) together, then every lane
+// issues all of its 16-byte loads for the R rows before the first store, so
+// one memory round trip moves R rows.
+template <typename T, bool VEC, int R>
 __global__ void __launch_bounds__(kThreadsPerBlock)
     gather_rows_kernel(const T* __restrict__ x, long long ldx, int H,
                        const int32_t* __restrict__ map, int div, long long rows,
@@ -102,42 +104,66 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
   if (rows_dev != nullptr) nrows = min(nrows, static_cast<long long>(*rows_dev));
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       r < nrows; r += warps) {
-    const int a = __ldg(map + r);
-    T* orow = out + r * ldo;
+  const long long wid = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long long r0 = wid * R; r0 < nrows; r0 += warps * R) {
+    // lane i < R: map entry and weight of row r0 + i
+    int my_a = -1;
+    float my_w = 1.f;
+    if (lane < R && r0 + lane < nrows) {
+      my_a = __ldg(map + r0 + lane);
+      if (w != nullptr && my_a >= 0) my_w = V8<T>::to_f(w[my_a]);
+    }
+    int a[R];
+    float sc[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      a[i] = __shfl_sync(0xffffffffu, my_a, i);
+      sc[i] = __shfl_sync(0xffffffffu, my_w, i);
+    }
     if constexpr (VEC) {
-      const T* xrow = a >= 0 ? x + static_cast<long long>(a / div) * ldx : nullptr;
-      const float sc = (a >= 0 && w != nullptr) ? V8<T>::to_f(w[a]) : 1.f;
       for (int c0 = 0; c0 < H; c0 += 32 * 8 * kVecPerLane) {
-        uint4 u[kVecPerLane];
+        uint4 u[R][kVecPerLane];
 #pragma unroll
-        for (int j = 0; j < kVecPerLane; ++j) {
-          const int c = c0 + (j * 32 + lane) * 8;
-          u[j] = make_uint4(0, 0, 0, 0);
-          if (xrow != nullptr && c < H) u[j] = __ldg(reinterpret_cast<const uint4*>(xrow + c));
-        }
+        for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int j = 0; j < kVecPerLane; ++j) {
-          const int c = c0 + (j * 32 + lane) * 8;
-          if (c >= H) break;
-          if (w != nullptr && xrow != nullptr) {
-            float f[8];
-            V8<T>::load(u[j], f);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) f[q] *= sc;
-            u[j] = V8<T>::store(f);
+          for (int j = 0; j < kVecPerLane; ++j) {
+            const int c = c0 + (j * 32 + lane) * 8;
+            u[i][j] = make_uint4(0, 0, 0, 0);
+            if (a[i] >= 0 && c < H)
+              u[i][j] = __ldg(reinterpret_cast<const uint4*>(
+                  x + static_cast<long long>(a[i] / div) * ldx + c));
           }
-          *reinterpret_cast<uint4*>(orow + c) = u[j];
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          if (r0 + i >= nrows) break;
+          T* orow = out + (r0 + i) * ldo;
+#pragma unroll
+          for (int j = 0; j < kVecPerLane; ++j) {
+            const int c = c0 + (j * 32 + lane) * 8;
+            if (c >= H) break;
+            if (w != nullptr && a[i] >= 0) {
+              float f[8];
+              V8<T>::load(u[i][j], f);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) f[q] *= sc[i];
+              u[i][j] = V8<T>::store(f);
+            }
+            *reinterpret_cast<uint4*>(orow + c) = u[i][j];
+          }
         }
       }
     } else {
-      for (int c = lane; c < H; c += 32) {
-        if (a < 0) {
-          orow[c] = V8<T>::from_f(0.f);
-        } else {
-          const T v = x[static_cast<long long>(a / div) * ldx + c];
-          orow[c] = w ? V8<T>::from_f(V8<T>::to_f(v) * V8<T>::to_f(w[a])) : v;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        if (r0 + i >= nrows) break;
+        T* orow = out + (r0 + i) * ldo;
+        for (int c = lane; c < H; c += 32) {
+          if (a[i] < 0) {
+            orow[c] = V8<T>::from_f(0.f);
+          } else {
+            const T v = x[static_cast<long long>(a[i] / div) * ldx + c];
+            orow[c] = w ? V8<T>::from_f(V8<T>::to_f(v) * sc[i]) : v;
+          }
         }
       }
     }
@@ -146,79 +172,110 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
 }
 
 // out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding).
-// One warp per token; the k source rows' vectors are all loaded before any is
-// used.
-template <typename T, bool VEC, int kMaxK>
+// A warp combines R tokens at a time: lanes fetch the R * kMaxK row indices
+// and weights together, then all source-row vectors are loaded before any is
+// used.  Top-k beyond kMaxK runs in further batches of kMaxK.
+template <typename T, bool VEC, int kMaxK, int R>
 __global__ void __launch_bounds__(kThreadsPerBlock)
     combine_kernel(const T* __restrict__ y, long long ldy, int H,
                    const int32_t* __restrict__ asg_row, long long T_tokens, int k,
                    const T* __restrict__ w, T* __restrict__ out, long long ldo) {
+  static_assert(R * kMaxK <= 32, "one lane per (token, source row)");
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  constexpr int NV = VEC ? (kMaxK <= 2 ? 4 : 2) : 1;  // vectors per lane per batch
-  for (long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       t < T_tokens; t += warps) {
-    T* orow = out + t * ldo;
+  const long long wid = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  constexpr int NV = VEC ? 2 : 1;  // 16-byte vectors per lane per source row and batch
+  for (long long t0 = wid * R; t0 < T_tokens; t0 += warps * R) {
     if constexpr (VEC) {
       for (int c0 = 0; c0 < H; c0 += 32 * 8 * NV) {
-        float acc[NV][8];
+        float acc[R][NV][8];
 #pragma unroll
-        for (int v = 0; v < NV; ++v)
+        for (int i = 0; i < R; ++i)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc[v][q] = 0.f;
-        for (int j0 = 0; j0 < k; j0 += kMaxK) {  // top-k beyond kMaxK: more batches
+          for (int v = 0; v < NV; ++v)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[i][v][q] = 0.f;
+        for (int j0 = 0; j0 < k; j0 += kMaxK) {
           const int kk = min(kMaxK, k - j0);
-          int rows[kMaxK];
-          float sc[kMaxK];
-          uint4 u[kMaxK][NV];
-#pragma unroll
-          for (int j = 0; j < kMaxK; ++j) {
-            rows[j] = j < kk ? __ldg(asg_row + t * k + j0 + j) : -1;
-            sc[j] = (j < kk && w != nullptr) ? V8<T>::to_f(w[t * k + j0 + j]) : 1.f;
-          }
-#pragma unroll
-          for (int j = 0; j < kMaxK; ++j)
-#pragma unroll
-            for (int v = 0; v < NV; ++v) {
-              const int c = c0 + (v * 32 + lane) * 8;
-              if (rows[j] >= 0 && c < H)
-                u[j][v] = __ldg(reinterpret_cast<const uint4*>(y + rows[j] * ldy + c));
+          // lane l < R * kMaxK: source row and weight of (token l / kMaxK, j0 + l % kMaxK)
+          int my_row = -1;
+          float my_sc = 1.f;
+          {
+            const int ti = lane / kMaxK, jj = lane % kMaxK;
+            if (lane < R * kMaxK && jj < kk && t0 + ti < T_tokens) {
+              const long long ai = (t0 + ti) * k + j0 + jj;
+              my_row = __ldg(asg_row + ai);
+              if (w != nullptr) my_sc = V8<T>::to_f(w[ai]);
             }
+          }
+          int rows[R][kMaxK];
+          float sc[R][kMaxK];
 #pragma unroll
-          for (int j = 0; j < kMaxK; ++j) {
-            if (rows[j] < 0) continue;
+          for (int i = 0; i < R; ++i)
 #pragma unroll
-            for (int v = 0; v < NV; ++v) {
-              if (c0 + (v * 32 + lane) * 8 >= H) continue;
-              float f[8];
-              V8<T>::load(u[j][v], f);
-              if (w != nullptr) {
+            for (int j = 0; j < kMaxK; ++j) {
+              rows[i][j] = __shfl_sync(0xffffffffu, my_row, i * kMaxK + j);
+              sc[i][j] = __shfl_sync(0xffffffffu, my_sc, i * kMaxK + j);
+            }
+          uint4 u[R][kMaxK][NV];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) acc[v][q] += V8<T>::rnd(f[q] * sc[j]);
-              } else {
+          for (int i = 0; i < R; ++i)
 #pragma unroll
-                for (int q = 0; q < 8; ++q) acc[v][q] += f[q];
+            for (int j = 0; j < kMaxK; ++j)
+#pragma unroll
+              for (int v = 0; v < NV; ++v) {
+                const int c = c0 + (v * 32 + lane) * 8;
+                if (rows[i][j] >= 0 && c < H)
+                  u[i][j][v] = __ldg(reinterpret_cast<const uint4*>(y + rows[i][j] * ldy + c));
+              }
+#pragma unroll
+          for (int i = 0; i < R; ++i)
+#pragma unroll
+            for (int j = 0; j < kMaxK; ++j) {
+              if (rows[i][j] < 0) continue;
+#pragma unroll
+              for (int v = 0; v < NV; ++v) {
+                if (c0 + (v * 32 + lane) * 8 >= H) continue;
+                float f[8];
+                V8<T>::load(u[i][j][v], f);
+                if (w != nullptr) {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) acc[i][v][q] += V8<T>::rnd(f[q] * sc[i][j]);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) acc[i][v][q] += f[q];
+                }
               }
             }
-          }
         }
 #pragma unroll
-        for (int v = 0; v < NV; ++v) {
-          const int c = c0 + (v * 32 + lane) * 8;
-          if (c < H) *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(acc[v]);
+        for (int i = 0; i < R; ++i) {
+          if (t0 + i >= T_tokens) break;
+          T* orow = out + (t0 + i) * ldo;
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            const int c = c0 + (v * 32 + lane) * 8;
+            if (c < H) *reinterpret_cast<uint4*>(orow + c) = V8<T>::store(acc[i][v]);
+          }
         }
       }
     } else {
-      for (int c = lane; c < H; c += 32) {
-        float acc = 0.f;
-        for (int j = 0; j < k; ++j) {
-          const int row = __ldg(asg_row + t * k + j);
-          if (row < 0) continue;
-          const float v = V8<T>::to_f(y[row * ldy + c]);
-          acc += (w != nullptr) ? V8<T>::rnd(v * V8<T>::to_f(w[t * k + j])) : v;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const long long t = t0 + i;
+        if (t >= T_tokens) break;
+        T* orow = out + t * ldo;
+        for (int c = lane; c < H; c += 32) {
+          float acc = 0.f;
+          for (int j = 0; j < k; ++j) {
+            const int row = __ldg(asg_row + t * k + j);
+            if (row < 0) continue;
+            const float v = V8<T>::to_f(y[row * ldy + c]);
+            acc += (w != nullptr) ? V8<T>::rnd(v * V8<T>::to_f(w[t * k + j])) : v;
+          }
+          orow[c] = V8<T>::from_f(acc);
         }
-        orow[c] = V8<T>::from_f(acc);
       }
     }
   }
@@ -307,13 +364,15 @@ int gather_t(const void* x, long long ldx, int H, const int32_t* map, int div, l
   const T* xp = static_cast<const T*>(x);
   const T* wp = static_cast<const T*>(w);
   T* op = static_cast<T*>(out);
+  constexpr int R = 1;  // rows per warp batch (more rows per warp measured slower)
+  const int grid = grid_for((rows + R - 1) / R, kThreadsPerBlock / 32);
   if constexpr (sizeof(T) == 2) {
     if (vec)
-      return launch_pdl(gather_rows_kernel<T, true>, grid_for(rows, kThreadsPerBlock / 32),
-                        st, xp, ldx, H, map, div, rows, rows_dev, wp, op, ldo);
+      return launch_pdl(gather_rows_kernel<T, true, R>, grid, st, xp, ldx, H, map, div, rows,
+                        rows_dev, wp, op, ldo);
   }
-  return launch_pdl(gather_rows_kernel<T, false>, grid_for(rows, kThreadsPerBlock / 32), st, xp,
-                    ldx, H, map, div, rows, rows_dev, wp, op, ldo);
+  return launch_pdl(gather_rows_kernel<T, false, R>, grid, st, xp, ldx, H, map, div, rows,
+                    rows_dev, wp, op, ldo);
 }
 
 template <typename T>
@@ -324,23 +383,22 @@ int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long 
   const T* yp = static_cast<const T*>(y);
   const T* wp = static_cast<const T*>(w);
   T* op = static_cast<T*>(out);
-  // source-row arrays sized to top_k (registers bound the resident blocks)
-  const int grid_v = grid_for(T_tokens, kThreadsPerBlock / 32);
-  const int grid_s = grid_v;
-#define MOE_COMBINE(KM)                                                                       \
+  // tokens per warp batch: R * kMaxK source rows in flight (at most 8)
+#define MOE_COMBINE(KM, R)                                                                     \
   do {                                                                                         \
+    const int grid = grid_for((T_tokens + (R) - 1) / (R), kThreadsPerBlock / 32);              \
     if constexpr (sizeof(T) == 2) {                                                            \
       if (vec)                                                                                 \
-        return launch_pdl(combine_kernel<T, true, KM>, grid_v, st, yp, ldy, H, asg_row,        \
+        return launch_pdl(combine_kernel<T, true, KM, R>, grid, st, yp, ldy, H, asg_row,       \
                           T_tokens, k, wp, op, ldo);                                           \
     }                                                                                          \
-    return launch_pdl(combine_kernel<T, false, KM>, grid_s, st, yp, ldy, H, asg_row, T_tokens, \
+    return launch_pdl(combine_kernel<T, false, KM, R>, grid, st, yp, ldy, H, asg_row, T_tokens, \
                       k, wp, op, ldo);                                                         \
   } while (0)
-  if (k <= 1) MOE_COMBINE(1);
-  if (k <= 2) MOE_COMBINE(2);
-  if (k <= 4) MOE_COMBINE(4);
-  MOE_COMBINE(8);
+  if (k <= 1) MOE_COMBINE(1, 2);
+  if (k <= 2) MOE_COMBINE(2, 2);
+  if (k <= 4) MOE_COMBINE(4, 1);
+  MOE_COMBINE(8, 1);
 #undef MOE_COMBINE
 }
 

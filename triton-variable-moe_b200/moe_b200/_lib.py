@@ -30,6 +30,7 @@ STATUS_TEXT = {
 DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 ACT_CODE = {"none": 0, "relu_squared": 1}
 ROUND_CODE = {"up": 0, "down": 1, "nearest": 2}
+TILE_PAIR = 0x200  # tile_n flag: 256-row tiles on SM pairs (2-CTA clusters)
 
 _P = c_void_p
 _I = c_int

@@ -290,7 +290,7 @@ class ExpertParallelMoEMLP(nn.Module):
         p = self._plan_cache
         if p is None or p.local.w_off is not self.local_weight_offsets:
             lw = self._local_widths
-            tn_w = 256 if all(w % 256 == 0 for w in lw) else 128
+            tn_w = 256 if max(lw, default=0) > 128 else 128
             tn_h = 256 if self.config.n_embd % 256 == 0 else 128
             local = _Plan(len(lw), 1, self.block_size, self.config.n_embd, max(lw),
                           self.local_weight_offsets, tn_w, tn_h)

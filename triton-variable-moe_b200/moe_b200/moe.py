@@ -295,7 +295,9 @@ class TritonMoEMLP(nn.Module):
         p = self._plan_cache
         w_off = self.expert_weight_offsets_t
         if p is None or p.w_off is not w_off:
-            tn_w = 256 if all(w % 256 == 0 for w in self.expert_widths) else 128
+            # N tile 256 once any expert is wider than 128 (narrower experts then
+            # leave part of a tile idle, which measured cheaper than twice the tiles)
+            tn_w = 256 if self.max_expert_width > 128 else 128
             tn_h = 256 if self.config.n_embd % 256 == 0 else 128
             p = _Plan(self.num_experts, self.num_active_experts, self.block_size,
                       self.config.n_embd, self.max_expert_width, w_off, tn_w, tn_h)
