@@ -135,11 +135,15 @@ MOE_API int moe_router_topk(const float* router_probs, int64_t num_tokens, int n
  *   lse [T] fp32 = logsumexp(logits_t) with torch's rounding chain in the
  *   logits dtype; workspace (moe_router_head_workspace_floats floats):
  *   per-block partial sums for the losses.
+ * The workspace also receives each expert's selection count.
  * moe_aux_losses then forms losses[0] = router_z_loss (mean lse^2, rounded to
  * the logits dtype), losses[1] = load_balance_loss = sum_e lb_coef[e] * f_i[e]
  * * p_i[e], losses[2] = compute_loss = mean_t sum_e probs * widths_normalized,
  * f_i [E] = tokens_per_expert / sum (f_dtype) and p_i [E] fp32 = mean probs;
  * z_loss (nullable) receives router_z_loss in the logits dtype.
+ * tokens_per_expert may be NULL: the head's own selection counts are used
+ * (equal to fused_route's tokens_per_expert for the same selections), so the
+ * losses do not wait for routing.
  */
 MOE_API int64_t moe_router_head_workspace_floats(int64_t num_tokens, int num_experts);
 MOE_API int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tokens,
@@ -147,6 +151,21 @@ MOE_API int moe_router_head(const void* router_logits, int logits_dtype, int64_t
                             const float* widths_normalized, float* router_probs, void* weights,
                             int weights_dtype, int32_t* selected_experts, float* lse,
                             float* workspace, void* stream);
+/*
+ * moe_router_head and moe_aux_losses in one launch (no counterpart in the
+ * reference, which computes these in torch): the head also counts each
+ * expert's selections (= tokens_per_expert), and its last block to finish
+ * forms losses / f_i / p_i / z_loss as moe_aux_losses does.  f_i has the
+ * weights dtype.  ticket: a device word that is zero before the first call;
+ * every call leaves it zero again.  Calls sharing a ticket must not overlap.
+ */
+MOE_API int moe_router_head_losses(const void* router_logits, int logits_dtype,
+                                   int64_t num_tokens, int num_experts, int top_k, int normalize,
+                                   const float* widths_normalized, float* router_probs,
+                                   void* weights, int weights_dtype, int32_t* selected_experts,
+                                   float* lse, float* workspace, const float* lb_coef,
+                                   float* losses, void* f_i, float* p_i, void* z_loss,
+                                   unsigned* ticket, void* stream);
 MOE_API int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,
                            const int32_t* tokens_per_expert, const float* lb_coef,
                            int logits_dtype, float* losses, void* f_i, int f_dtype, float* p_i,

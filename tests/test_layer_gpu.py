@@ -127,13 +127,10 @@ def test_aux_losses_match_reference_formulas(device):
     with torch.no_grad():
         m.router.weight.copy_(torch.from_numpy(d["router_w"]))
     x = torch.from_numpy(d["x"]).to(device)
-    logits, probs, w, sel, lse, ws = m._route_weights(x.reshape(-1, H))
+    logits, probs, w, sel, lse, head_losses = m._route_weights(x.reshape(-1, H))
     np.testing.assert_array_equal(sel.reshape(-1).cpu().numpy(), d["selected"])
     np.testing.assert_allclose(w.reshape(-1).cpu().numpy(), d["weights"], rtol=1e-6, atol=1e-7)
-    from moe_b200.kernels import fused_route
-
-    _, _, tpe, _, _ = fused_route(torch.from_numpy(d["selected"]).to(device), m.num_experts)
-    aux, f_i = m._aux_losses(logits, lse, ws, probs, tpe, torch.float32)
+    aux, f_i = m._aux_losses(logits, lse, head_losses, probs)
     np.testing.assert_allclose(f_i.cpu().numpy(), d["f_i"], rtol=1e-6)
     np.testing.assert_allclose(aux["router_z_loss"].item(), d["z_loss"], rtol=1e-5)
     np.testing.assert_allclose(aux["load_balance_loss"].item(), d["lb_loss"], rtol=1e-5)
@@ -149,11 +146,11 @@ def test_aux_losses_forward_and_gradients_match_torch(sizes, dtype, device):
     E = sum(c for c, _ in sizes)
     m = make_layer(H, sizes, min(k, E), 64, device=device, dtype=dtype)
     x = torch.randn(300, H, device=device, dtype=dtype)
-    logits, probs, w, sel, lse, ws = m._route_weights(x)
+    logits, probs, w, sel, lse, head_losses = m._route_weights(x)
     from moe_b200.kernels import fused_route
 
     _, _, tpe, _, _ = fused_route(sel.reshape(-1), E)
-    aux, f_i = m._aux_losses(logits, lse, ws, probs, tpe, dtype)
+    aux, f_i = m._aux_losses(logits, lse, head_losses, probs)
     (aux["router_z_loss"].float() + aux["load_balance_loss"] + aux["compute_loss"]).backward()
     g_fused = m.router.weight.grad.float().clone()
     m.router.weight.grad = None
@@ -167,6 +164,36 @@ def test_aux_losses_forward_and_gradients_match_torch(sizes, dtype, device):
     for key in aux:
         torch.testing.assert_close(aux[key].float(), ref[key].float(), rtol=tol, atol=1e-6)
     torch.testing.assert_close(g_fused, g_ref, rtol=5e-2, atol=1e-2 * g_ref.abs().max().item())
+
+
+@pytest.mark.parametrize("T,E,k", [(300, 6, 2), (8192, 16, 2), (20000, 64, 8), (5, 3, 1)])
+def test_fused_head_losses_match_separate_launches(T, E, k, device):
+    """moe_router_head_losses (head + losses in one launch, expert counts taken
+    from the head's own selections) equals moe_router_head + moe_aux_losses with
+    the routing's tokens_per_expert, and leaves its ticket at zero."""
+    from moe_b200.kernels import _ops, fused_route
+
+    g = torch.Generator(device="cpu").manual_seed(T + E)
+    logits = torch.randn(T, E, generator=g).to(device, torch.bfloat16)
+    wn = torch.rand(E, generator=g).to(device)
+    coef = torch.rand(E, generator=g).to(device)
+    ticket = torch.zeros(1, dtype=torch.int32, device=device)
+    for _ in range(3):  # the ticket is reused across calls
+        probs, w, sel, lse, ws, (losses, f_i, p_i, z) = _ops.router_head(
+            logits, k, True, torch.bfloat16, wn, coef, ticket)
+        probs2, w2, sel2, lse2, ws2 = _ops.router_head(logits, k, True, torch.bfloat16, wn)
+        _, _, tpe, _, _ = fused_route(sel2.reshape(-1), E)
+        losses2, f2, p2, z2 = _ops.aux_losses(ws2, T, tpe, coef, torch.bfloat16, torch.bfloat16)
+        # the head's own selection counts stand in for tokens_per_expert
+        losses3, f3, p3, z3 = _ops.aux_losses(ws2, T, None, coef, torch.bfloat16, torch.bfloat16)
+        torch.cuda.synchronize()
+        assert torch.equal(losses3, losses2) and torch.equal(f3, f2) and torch.equal(z3, z2)
+        assert int(ticket.item()) == 0
+        assert torch.equal(sel, sel2) and torch.equal(w, w2) and torch.equal(probs, probs2)
+        assert torch.equal(f_i, f2)
+        torch.testing.assert_close(p_i, p2, rtol=1e-6, atol=0)
+        torch.testing.assert_close(losses, losses2, rtol=1e-6, atol=0)
+        assert torch.equal(z, z2)
 
 
 def test_state_dict_layout_matches_reference(device):

@@ -25,7 +25,8 @@ int router_topk(const float* probs, long long T, int E, int k, int norm, void* w
 int router_head_blocks(long long T);
 int router_head(const void* logits, int l_dtype, long long T, int E, int k, int norm,
                 const float* widths_norm, float* probs, void* w, int w_dtype, int32_t* sel,
-                float* lse, float* partials, int nblocks, cudaStream_t st);
+                float* lse, float* partials, int nblocks, const float* lb_coef, float* losses,
+                void* f_i, float* p_i, void* z_out, unsigned* ticket, cudaStream_t st);
 int aux_finalize(const float* partials, int nblocks, int E, long long T, const int32_t* tpe,
                  const float* lb_coef, int l_dtype, float* losses, void* f_i, int f_dtype,
                  float* p_i, void* z_out, cudaStream_t st);
@@ -143,7 +144,7 @@ int moe_router_topk(const float* router_probs, int64_t num_tokens, int num_exper
 
 int64_t moe_router_head_workspace_floats(int64_t num_tokens, int num_experts) {
   if (num_tokens < 0 || num_experts <= 0) return 0;
-  return static_cast<int64_t>(moe::router_head_blocks(num_tokens)) * (num_experts + 2);
+  return static_cast<int64_t>(moe::router_head_blocks(num_tokens)) * (2 * num_experts + 2);
 }
 
 int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tokens,
@@ -154,7 +155,20 @@ int moe_router_head(const void* router_logits, int logits_dtype, int64_t num_tok
   return moe::router_head(router_logits, logits_dtype, num_tokens, num_experts, top_k, normalize,
                           widths_normalized, router_probs, weights, weights_dtype,
                           selected_experts, lse, workspace, moe::router_head_blocks(num_tokens),
-                          S(stream));
+                          nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, S(stream));
+}
+
+int moe_router_head_losses(const void* router_logits, int logits_dtype, int64_t num_tokens,
+                           int num_experts, int top_k, int normalize,
+                           const float* widths_normalized, float* router_probs, void* weights,
+                           int weights_dtype, int32_t* selected_experts, float* lse,
+                           float* workspace, const float* lb_coef, float* losses, void* f_i,
+                           float* p_i, void* z_loss, unsigned* ticket, void* stream) {
+  if (num_tokens <= 0 || losses == nullptr) return MOE_ERR_BAD_ARG;
+  return moe::router_head(router_logits, logits_dtype, num_tokens, num_experts, top_k, normalize,
+                          widths_normalized, router_probs, weights, weights_dtype,
+                          selected_experts, lse, workspace, moe::router_head_blocks(num_tokens),
+                          lb_coef, losses, f_i, p_i, z_loss, ticket, S(stream));
 }
 
 int moe_aux_losses(const float* workspace, int64_t num_tokens, int num_experts,

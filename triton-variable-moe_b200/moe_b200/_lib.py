@@ -46,6 +46,8 @@ _SIGS = {
     "moe_router_topk": [_P, _L, _I, _I, _I, _P, _I, _P, _P],
     "moe_router_head_workspace_floats": [_L, _I],
     "moe_router_head": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P],
+    "moe_router_head_losses": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,
+                               _P, _P, _P],
     "moe_aux_losses": [_P, _L, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P],
     "moe_build_row_map": [_P, _P, _P, _P, _L, _L, _P, _L, _P, _P, _P],
     "moe_gather_map": [_P, _L, _I, _P, _P],

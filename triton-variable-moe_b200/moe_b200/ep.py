@@ -250,6 +250,7 @@ class ExpertParallelMoEMLP(nn.Module):
     def _lb_coef(self, device) -> torch.Tensor:
         return TritonMoEMLP._lb_coef(self, device)
 
+
     def _slice(self, w1_full: torch.Tensor, w2_full: torch.Tensor):
         offs = [0]
         for w in self.expert_widths:
@@ -307,11 +308,14 @@ class ExpertParallelMoEMLP(nn.Module):
         x_flat = x.reshape(B * S, H)
         logits = self.router(x_flat)
         wn = self.expert_widths_normalized.float()
-        probs, w, sel, lse, ws = _RouterHead.apply(logits, self.num_active_experts,
-                                                   self.norm_topk_prob, x_flat.dtype, wn)
-        out_flat, tpe = _EPMoEFunction.apply(x_flat.to(self.w1.dtype), self.w1, self.w2,
-                                             w.reshape(-1), sel.reshape(-1), self._plan())
-        z, lb, cl, f_i = _AuxLosses.apply(logits, probs, lse, ws, tpe.to(torch.int32),
-                                          self._lb_coef(logits.device), wn, x.dtype)
+        # the auxiliary losses use this rank's token counts per expert, which the
+        # router head counts itself from its selections
+        probs, w, sel, lse, losses, f_i, z = _RouterHead.apply(
+            logits, self.num_active_experts, self.norm_topk_prob, x_flat.dtype, wn,
+            self._lb_coef(logits.device), None)
+        out_flat, _tpe = _EPMoEFunction.apply(x_flat.to(self.w1.dtype), self.w1, self.w2,
+                                              w.reshape(-1), sel.reshape(-1), self._plan())
+        z, lb, cl, f_i = _AuxLosses.apply(logits, probs, lse, losses, f_i, z,
+                                          self._lb_coef(logits.device), wn)
         aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
         return out_flat.reshape(B, S, -1), aux, f_i

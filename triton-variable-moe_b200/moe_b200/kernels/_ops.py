@@ -173,9 +173,13 @@ def router_topk(router_probs: torch.Tensor, top_k: int, normalize: bool, weights
 
 
 def router_head(router_logits: torch.Tensor, top_k: int, normalize: bool,
-                weights_dtype: torch.dtype, widths_normalized: torch.Tensor):
+                weights_dtype: torch.dtype, widths_normalized: torch.Tensor,
+                lb_coef: torch.Tensor | None = None, ticket: torch.Tensor | None = None):
     """One pass over the router logits: (probs fp32 [T,E], top-k weights [T,k],
-    selected int32 [T,k], per-token logsumexp fp32 [T], loss partials)."""
+    selected int32 [T,k], per-token logsumexp fp32 [T], loss partials).  With
+    lb_coef and ticket (a zeroed int32 device word the kernel returns to zero)
+    the same launch also forms the auxiliary losses; then (losses fp32 [3],
+    f_i [E] in weights_dtype, p_i fp32 [E], z-loss in the logits dtype) follow."""
     require_cuda(router_logits)
     lg = router_logits.contiguous()
     T, E = lg.shape
@@ -187,29 +191,49 @@ def router_head(router_logits: torch.Tensor, top_k: int, normalize: bool,
     ws = torch.empty(max(int(lib.moe_router_head_workspace_floats(T, E)), 1), dtype=torch.float32,
                      device=dev)
     wn = widths_normalized.float().contiguous()
+    fused = lb_coef is not None and T > 0
     ev = _ev_begin()
-    rc = lib.moe_router_head(ptr(lg), DTYPE_CODE[lg.dtype], T, E, int(top_k),
-                             1 if normalize else 0, ptr(wn), ptr(probs), ptr(w),
-                             DTYPE_CODE[weights_dtype], ptr(sel), ptr(lse), ptr(ws),
-                             stream_handle(dev))
+    if fused:
+        losses = torch.empty(3, dtype=torch.float32, device=dev)
+        z = torch.empty((), dtype=lg.dtype, device=dev)
+        f_i = torch.empty(E, dtype=weights_dtype, device=dev)
+        p_i = torch.empty(E, dtype=torch.float32, device=dev)
+        rc = lib.moe_router_head_losses(
+            ptr(lg), DTYPE_CODE[lg.dtype], T, E, int(top_k), 1 if normalize else 0, ptr(wn),
+            ptr(probs), ptr(w), DTYPE_CODE[weights_dtype], ptr(sel), ptr(lse), ptr(ws),
+            ptr(lb_coef.float().contiguous()), ptr(losses), ptr(f_i), ptr(p_i), ptr(z),
+            ptr(ticket), stream_handle(dev))
+        name = "moe_router_head_losses"
+    else:
+        rc = lib.moe_router_head(ptr(lg), DTYPE_CODE[lg.dtype], T, E, int(top_k),
+                                 1 if normalize else 0, ptr(wn), ptr(probs), ptr(w),
+                                 DTYPE_CODE[weights_dtype], ptr(sel), ptr(lse), ptr(ws),
+                                 stream_handle(dev))
+        name = "moe_router_head"
     _ev_end(ev, "router_head")
-    check(rc, "moe_router_head")
+    check(rc, name)
     _count(1)
+    if fused:
+        return probs, w, sel, lse, ws, (losses, f_i, p_i, z)
     return probs, w, sel, lse, ws
 
 
-def aux_losses(ws: torch.Tensor, num_tokens: int, tokens_per_expert: torch.Tensor,
-               lb_coef: torch.Tensor, logits_dtype: torch.dtype, f_dtype: torch.dtype):
+def aux_losses(ws: torch.Tensor, num_tokens: int, tokens_per_expert: torch.Tensor | None,
+               lb_coef: torch.Tensor, logits_dtype: torch.dtype, f_dtype: torch.dtype,
+               out: tuple | None = None):
     """(losses fp32 [3] = z, load balance, compute; f_i [E]; p_i fp32 [E];
-    z-loss in the logits dtype)."""
+    z-loss in the logits dtype).  tokens_per_expert None: the router head's own
+    selection counts in ws are used.  out: preallocated (losses, f_i, p_i, z)."""
     dev = ws.device
-    E = tokens_per_expert.numel()
-    losses = torch.empty(3, dtype=torch.float32, device=dev)
-    z = torch.empty((), dtype=logits_dtype, device=dev)
-    f_i = torch.empty(E, dtype=f_dtype, device=dev)
-    p_i = torch.empty(E, dtype=torch.float32, device=dev)
+    E = lb_coef.numel()
+    if out is None:
+        out = (torch.empty(3, dtype=torch.float32, device=dev), torch.empty(E, dtype=f_dtype, device=dev),
+               torch.empty(E, dtype=torch.float32, device=dev),
+               torch.empty((), dtype=logits_dtype, device=dev))
+    losses, f_i, p_i, z = out
+    tpe = _meta(tokens_per_expert) if tokens_per_expert is not None else None
     ev = _ev_begin()
-    rc = lib.moe_aux_losses(ptr(ws), int(num_tokens), E, ptr(_meta(tokens_per_expert)),
+    rc = lib.moe_aux_losses(ptr(ws), int(num_tokens), E, ptr(tpe),
                             ptr(lb_coef.float().contiguous()), DTYPE_CODE[logits_dtype],
                             ptr(losses), ptr(f_i), DTYPE_CODE[f_dtype], ptr(p_i), ptr(z),
                             stream_handle(dev))

@@ -143,41 +143,57 @@ class _MoEMLPFunction(torch.autograd.Function):
 
 
 class _RouterHead(torch.autograd.Function):
-    """sigmoid + top-k + renorm + per-token logsumexp of the router logits in one
-    kernel.  Differentiable output: the fp32 probabilities (d sigmoid = p(1-p))."""
+    """sigmoid + top-k + renorm + per-token logsumexp of the router logits (one
+    kernel), then the auxiliary losses from its partial sums and selection
+    counts (a second one-block kernel, on `aux_stream` when given so that it
+    overlaps the routing and expert GEMMs; the caller joins that stream before
+    the loss values are used).  Differentiable output: the fp32 probabilities
+    (d sigmoid = p(1-p)); the loss values are handed to _AuxLosses, which
+    carries their gradients."""
 
     @staticmethod
-    def forward(ctx, logits, top_k, normalize, weights_dtype, widths_normalized):
+    def forward(ctx, logits, top_k, normalize, weights_dtype, widths_normalized, lb_coef,
+                aux_stream):
         ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
         probs, w, sel, lse, ws = _ops.router_head(logits, top_k, normalize, weights_dtype,
                                                   widths_normalized)
+        T, E = logits.shape
+        dev = logits.device
+        out = (torch.empty(3, dtype=torch.float32, device=dev),
+               torch.empty(E, dtype=weights_dtype, device=dev),
+               torch.empty(E, dtype=torch.float32, device=dev),
+               torch.empty((), dtype=logits.dtype, device=dev))
+        if aux_stream is None:
+            _ops.aux_losses(ws, T, None, lb_coef, logits.dtype, weights_dtype, out=out)
+        else:
+            aux_stream.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(aux_stream):
+                _ops.aux_losses(ws, T, None, lb_coef, logits.dtype, weights_dtype, out=out)
+            ws.record_stream(aux_stream)
+        losses, f_i, _p_i, z = out
         ctx.save_for_backward(probs)
         ctx.logits_dtype = logits.dtype
-        ctx.mark_non_differentiable(w, sel, lse, ws)
-        return probs, w, sel, lse, ws
+        ctx.mark_non_differentiable(w, sel, lse, losses, f_i, z)
+        return probs, w, sel, lse, losses, f_i, z
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, g_probs, _w, _sel, _lse, _ws):
+    def backward(ctx, g_probs, _w, _sel, _lse, _losses, _f_i, _z):
         (probs,) = ctx.saved_tensors
         g = None
         if g_probs is not None:
             g = (g_probs * probs * (1.0 - probs)).to(ctx.logits_dtype)
-        return g, None, None, None, None
+        return g, None, None, None, None, None, None
 
 
 class _AuxLosses(torch.autograd.Function):
-    """router_z_loss, load_balance_loss, compute_loss and f_i from the partial
-    sums of the router head (one kernel).  Backward restates the gradients of
-    the reference's torch expressions (moe.py:253-303)."""
+    """router_z_loss, load_balance_loss, compute_loss and f_i as the router head
+    computed them (forward passes them through).  Backward restates the
+    gradients of the reference's torch expressions (moe.py:253-303)."""
 
     @staticmethod
-    def forward(ctx, logits, probs, lse, ws, tokens_per_expert, lb_coef, widths_normalized,
-                f_dtype):
+    def forward(ctx, logits, probs, lse, losses, f_i, z, lb_coef, widths_normalized):
         ctx.set_materialize_grads(False)  # no zero-filled grads for unused outputs
-        T = logits.shape[0]
-        losses, f_i, _p_i, z = _ops.aux_losses(ws, T, tokens_per_expert, lb_coef, logits.dtype,
-                                               f_dtype)
         lb = losses[1]
         cl = losses[2]
         ctx.save_for_backward(logits, lse, f_i, lb_coef, widths_normalized)
@@ -326,18 +342,36 @@ class TritonMoEMLP(nn.Module):
             cache[device] = t
         return t
 
-    def _route_weights(self, x_flat):
-        """(logits, probs, top-k weights, selected int32, lse, loss partials)."""
-        router_logits = self.router(x_flat)
-        router_probs, top_k_weights, selected, lse, ws = _RouterHead.apply(
-            router_logits, self.num_active_experts, self.norm_topk_prob, x_flat.dtype,
-            self._fp32("expert_widths_normalized"))
-        return router_logits, router_probs, top_k_weights, selected, lse, ws
+    def _aux_stream(self, device) -> torch.cuda.Stream:
+        """Side stream the auxiliary-loss kernel runs on (one per module and
+        device), so that it overlaps the routing and the expert GEMMs."""
+        cache = self.__dict__.setdefault("_aux_stream_cache", {})
+        s = cache.get(device)
+        if s is None:
+            s = torch.cuda.Stream(device=device)
+            cache[device] = s
+        return s
 
-    def _aux_losses(self, router_logits, lse, ws, router_probs, tokens_per_expert, dtype):
-        z, lb, cl, f_i = _AuxLosses.apply(router_logits, router_probs, lse, ws, tokens_per_expert,
+    def _route_weights(self, x_flat, overlap: bool = False):
+        """(logits, probs, top-k weights, selected int32, lse, (losses, f_i, z)),
+        the auxiliary losses from the router head's own selection counts (f_i in
+        x's dtype).  overlap: the loss kernel runs on the side stream; the caller
+        must join it (`_join_aux`) before using the loss values."""
+        router_logits = self.router(x_flat)
+        router_probs, top_k_weights, selected, lse, losses, f_i, z = _RouterHead.apply(
+            router_logits, self.num_active_experts, self.norm_topk_prob, x_flat.dtype,
+            self._fp32("expert_widths_normalized"), self._lb_coef(x_flat.device),
+            self._aux_stream(x_flat.device) if overlap else None)
+        return router_logits, router_probs, top_k_weights, selected, lse, (losses, f_i, z)
+
+    def _join_aux(self, device) -> None:
+        torch.cuda.current_stream(device).wait_stream(self._aux_stream(device))
+
+    def _aux_losses(self, router_logits, lse, head_losses, router_probs):
+        losses, f_i, z = head_losses
+        z, lb, cl, f_i = _AuxLosses.apply(router_logits, router_probs, lse, losses, f_i, z,
                                           self._lb_coef(router_logits.device),
-                                          self._fp32("expert_widths_normalized"), dtype)
+                                          self._fp32("expert_widths_normalized"))
         aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
         return aux, f_i
 
@@ -361,14 +395,15 @@ class TritonMoEMLP(nn.Module):
         """x: [batch, seq, n_embd] -> (output, aux_loss dict, f_i)."""
         batch_size, seq_len, n_embd = x.shape
         x_flat = x.reshape(batch_size * seq_len, n_embd)
-        router_logits, router_probs, top_k_weights, selected, lse, ws = self._route_weights(x_flat)
+        router_logits, router_probs, top_k_weights, selected, lse, head_losses = (
+            self._route_weights(x_flat, overlap=True))
         out_flat, tokens_per_expert = _MoEMLPFunction.apply(
             x_flat.to(self.w1.dtype), self.w1, self.w2, top_k_weights.reshape(-1),
             selected.reshape(-1), self._plan(),
         )
         output = out_flat.reshape(batch_size, seq_len, -1)
-        aux, f_i = self._aux_losses(router_logits, lse, ws, router_probs, tokens_per_expert,
-                                    x.dtype)
+        self._join_aux(x.device)
+        aux, f_i = self._aux_losses(router_logits, lse, head_losses, router_probs)
         return output, aux, f_i
 
     def _compute_load_balance_loss(self, router_probs: torch.Tensor, f_i: torch.Tensor) -> torch.Tensor:
@@ -444,7 +479,7 @@ class TritonMoEMLP(nn.Module):
         with profiler.step("flatten"):
             x_flat = x.reshape(batch_size * seq_len, n_embd)
         with profiler.step("routing"):
-            router_logits, router_probs, top_k_weights, selected_experts, lse, ws = (
+            router_logits, router_probs, top_k_weights, selected_experts, lse, head_losses = (
                 self._route_weights(x_flat))
             top_k_weights_flat = top_k_weights.reshape(-1)
             selected_experts_flat = selected_experts.reshape(-1)
@@ -471,6 +506,5 @@ class TritonMoEMLP(nn.Module):
         with profiler.step("reshape"):
             output = output_flat.reshape(batch_size, seq_len, -1)
         with profiler.step("aux_loss"):
-            aux, f_i = self._aux_losses(router_logits, lse, ws, router_probs, tokens_per_expert,
-                                        x.dtype)
+            aux, f_i = self._aux_losses(router_logits, lse, head_losses, router_probs)
         return output, aux, f_i
