@@ -58,8 +58,10 @@ CONFIGS = {
     "c3": dict(n_embd=768, expert_sizes=[(4, 512), (8, 256), (4, 128)], top_k=2, batch=8, seq=1024,
                zipf=False),
     "c4": dict(n_embd=2048, expert_sizes=[(64, 1024)], top_k=8, batch=1, seq=16384, zipf=True),
+    # the expert-parallel config: at N > 1 its experts are sharded over the GPUs;
+    # the others run as independent replicas at N > 1 (their experts fit one GPU)
     "c5": dict(n_embd=4096, expert_sizes=[(32, 2048), (64, 1024), (32, 512)], top_k=8, batch=1,
-               seq=65536, zipf=True),
+               seq=65536, zipf=True, ep=True),
 }
 
 
@@ -379,7 +381,8 @@ def run_b200(args, cfg, name):
 
     T = cfg["batch"] * cfg["seq"]
     H = cfg["n_embd"]
-    layer = build_layer(cfg, dev, seed=0) if ws == 1 else build_ep_layer(cfg, dev, seed=0)
+    ep = ws > 1 and cfg.get("ep", False)  # expert parallel; else one replica per GPU
+    layer = build_ep_layer(cfg, dev, seed=0) if ep else build_layer(cfg, dev, seed=0)
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
     x_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
     g_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
@@ -403,7 +406,7 @@ def run_b200(args, cfg, name):
         torch.cuda.synchronize()
         return 0
 
-    if ws == 1:
+    if not ep:
         graph, out_static, per_step_launches, _ = capture_step(layer, x, gout)
         for _ in range(3):
             graph.replay()
@@ -423,7 +426,7 @@ def run_b200(args, cfg, name):
     sampler.start()
     t_end = time.perf_counter() + 1.5
     while time.perf_counter() < t_end:
-        for _ in range(20 if ws == 1 else 2):
+        for _ in range(2 if ep else 20):
             run_step()
         torch.cuda.synchronize()
 
@@ -462,7 +465,7 @@ def run_b200(args, cfg, name):
         lg = layer.router(xf)
         sel = torch.topk(torch.sigmoid(lg.float()), cfg["top_k"], dim=-1).indices
         tpe = torch.bincount(sel.reshape(-1), minlength=layer.num_experts)
-        if ws > 1:  # GEMM FLOPs of this rank: rows it receives for its own experts
+        if ep:  # GEMM FLOPs of this rank: rows it receives for its own experts
             dist.all_reduce(tpe)
             mine = torch.zeros_like(tpe)
             mine[layer.local_experts] = 1
@@ -472,7 +475,7 @@ def run_b200(args, cfg, name):
     reps = 5
     per_kind: dict[str, float] = {}
     kernel_timing = "eager"
-    if ws == 1:
+    if not ep:
         # the graphed step again, with an event-record node around each of our
         # launches: device time per kernel without host launch overhead
         try:
@@ -534,7 +537,7 @@ def run_b200(args, cfg, name):
     # output back to pinned host memory; the copies run on their own streams so
     # step i's upload and step i-1's download overlap step i's compute (two
     # device slots).  The L2 flush still precedes each step's compute.
-    if ws == 1:
+    if not ep:
         slots = [(x, gout, graph, out_static)]
         x2 = torch.empty_like(x).requires_grad_(True)
         g2 = torch.empty_like(gout)
@@ -608,7 +611,7 @@ def run_b200(args, cfg, name):
     e2e_value = T * ws * args.steps / (e2e_ms / 1e3)
     torch.cuda.synchronize()
     e2e_ok = bool(torch.equal(out_host[(args.steps - 1) % 2],
-                              slots[(args.steps - 1) % 2][3].detach().cpu())) if ws == 1 else None
+                              slots[(args.steps - 1) % 2][3].detach().cpu())) if not ep else None
     nbytes = x_host.numel() * 2
 
     cpu = None
@@ -638,7 +641,9 @@ def run_b200(args, cfg, name):
                 "seq_len": cfg["seq"],
                 "parallelism": (f"expert parallel over {ws} GPUs ({layer.num_experts} experts "
                                 f"sharded, NCCL all-to-all dispatch/combine), {T} tokens per GPU")
-                if ws > 1 else "single GPU",
+                if ep else (f"{ws} independent replicas, {T} tokens each, no collective (the "
+                            "config's experts fit one GPU; expert parallelism is the c5 "
+                            "config)") if ws > 1 else "single GPU",
                 "l2": "flushed by a 256 MiB write between timed steps",
             },
             "roofline": roofline,
@@ -647,7 +652,7 @@ def run_b200(args, cfg, name):
             "kernel_timing": kernel_timing,
             "eager_ms_per_step": eager_ms,
             "execution": ("step captured once in a CUDA graph and replayed (eager time in "
-                          "eager_ms_per_step)") if ws == 1 else
+                          "eager_ms_per_step)") if not ep else
                          "eager (expert-parallel exchange sizes are read on the host)",
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
