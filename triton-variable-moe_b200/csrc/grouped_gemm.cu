@@ -349,10 +349,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish<CG>();
     tc_fence_before();
   }
-  // Everything above touched only this CTA's own resources; from here on the
-  // kernel reads and writes global memory that earlier kernels in the stream
-  // produce or consume, so wait for them (programmatic dependent launch).
-  griddep_wait();
+  // The slot table reads only the expert offset arrays, which no kernel of the
+  // stream writes after the routing: every kernel here lets its dependents
+  // launch only after its own programmatic-launch wait, so when this grid
+  // starts every kernel before its immediate predecessor has completed, the
+  // routing included.  Building the table before this grid's own wait overlaps
+  // it with the predecessor's tail.
   if (warp == 2) {
     // Per-(problem, expert) geometry and the tile prefix table: lane L owns a
     // contiguous chunk of slots, then a warp scan turns chunk sums into offsets.
@@ -402,6 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 31) tb.prefix[nge] = incl;
   }
   __syncthreads();
+  // from here on the kernel reads and writes global memory that the preceding
+  // kernel may produce or consume: wait for it (programmatic dependent launch)
+  griddep_wait();
   // a pair's barriers are initialised before either CTA signals the other's
   if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
