@@ -390,9 +390,10 @@ __global__ void __launch_bounds__(kSmallWarps * 32, 1)
 }
 
 long long unit_size(long long A) {
-  // at most 256 units; at least 256 assignments (8 warp-steps) per unit
+  // at most 256 units (the workspace bound); at least 64 assignments (two
+  // warp-steps) per unit, so mid-size problems spread over many warps
   long long U = (A + 255) / 256;
-  if (U < 256) U = 256;
+  if (U < 64) U = 64;
   return (U + 31) / 32 * 32;
 }
 
