@@ -50,6 +50,7 @@ extern "C" {
 
 #define MOE_ACT_NONE 0
 #define MOE_ACT_RELU_SQUARED 1
+#define MOE_ACT_SWIGLU 2 /* moe_grouped_gemm_up_swiglu */
 
 #define MOE_ROUND_UP 0
 #define MOE_ROUND_DOWN 1
@@ -239,6 +240,31 @@ MOE_API int moe_grouped_gemm_up(const void* x, int64_t rows, int64_t ld_x, const
                         const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert,
                         int num_experts, int activation, void* out, void* pre_act,
                         int64_t ld_out, int dtype, int tile_n, int* status, void* stream);
+
+/* grouped_gemm_up with activation "swiglu" (grouped_gemm.py:270-358,
+ * ACTIVATION == 2): expert e's w1 columns are its gate block then its up block,
+ * so expert_weight_offsets step by 2 w_e and total_width = sum 2 w_e.
+ * out[rows_e, :w_e] = silu(x @ gate_e) * (x @ up_e) from the fp32 accumulators;
+ * gate (the reference's pre_act) and up (nullable) receive the rounded
+ * projections for the backward.  out / gate / up share ld_out. */
+MOE_API int moe_grouped_gemm_up_swiglu(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                                       int64_t hidden, int64_t total_width,
+                                       const int32_t* expert_token_offsets,
+                                       const int32_t* expert_weight_offsets,
+                                       const int32_t* tokens_per_expert, int num_experts,
+                                       void* out, void* gate, void* up, int64_t ld_out,
+                                       int dtype, int tile_n, int* status, void* stream);
+
+/* SwiGLU backward through the activation (the reference's is a placeholder,
+ * grouped_gemm.py:768-789): with s = sigmoid(gate),
+ * grad_act[r, 0:w_e) = g * up * s * (1 + gate (1 - s)) and
+ * grad_act[r, w_e:2 w_e) = g * gate * s for the rows of each expert e
+ * (expert_weight_offsets in the 2 w_e layout); moe_grouped_gemm_up_dx / _dw /
+ * _backward over that layout then give dX and dW1. */
+MOE_API int moe_swiglu_grad(const void* grad_out, const void* gate, const void* up, int64_t rows,
+                            int64_t ld, const int32_t* expert_token_offsets,
+                            const int32_t* expert_weight_offsets, int num_experts,
+                            void* grad_act, int64_t ld_act, int dtype, void* stream);
 
 /* grouped_gemm_down (grouped_gemm.py:586-651, kernel :480-583):
  * out[rows_e] = inter[rows_e, :w_e] @ w2[w_e rows]. */

@@ -183,9 +183,35 @@ def grouped_gemm_up(x, w1, expert_token_offsets, expert_weight_offsets, max_expe
             out[r0:r1, : c1 - c0] = rnd(p * p)
         elif activation == "none":
             out[r0:r1, : c1 - c0] = rnd(z)
+        elif activation == "swiglu":
+            # grouped_gemm.py:296-358: the expert's columns are gate then up
+            # (width w = (c1 - c0) / 2); out = silu(gate) * up, pre_act = gate
+            w = (c1 - c0) // 2
+            gate, up = z[:, :w], z[:, w:]
+            pre[r0:r1, :w] = rnd(gate)
+            out[r0:r1, :w] = rnd(gate / (1.0 + np.exp(-gate)) * up)
         else:
             raise NotImplementedError(activation)
     return out, pre
+
+
+def swiglu_backward(grad_out, gate, up, expert_token_offsets, expert_weight_offsets, dtype="fp32"):
+    """The true gradient through out = silu(gate) * up (the reference's own
+    swiglu backward is a placeholder, grouped_gemm.py:768-789): returns
+    grad_act [P, 2 max_w] with [dgate | dup] in each expert's w1 column layout."""
+    rnd = rounder(dtype)
+    g = np.asarray(grad_out, np.float32)
+    gate = np.asarray(gate, np.float32)
+    up = np.asarray(up, np.float32)
+    P, maxw = g.shape
+    out = np.zeros((P, 2 * maxw), np.float32)
+    for e, r0, r1, c0, c1 in _experts(expert_token_offsets, expert_weight_offsets):
+        w = (c1 - c0) // 2
+        a, u, gg = gate[r0:r1, :w], up[r0:r1, :w], g[r0:r1, :w]
+        s = 1.0 / (1.0 + np.exp(-a))
+        out[r0:r1, :w] = rnd(gg * u * s * (1.0 + a * (1.0 - s)))
+        out[r0:r1, w : 2 * w] = rnd(gg * a * s)
+    return out
 
 
 def grouped_gemm_down(inter, w2, expert_token_offsets, expert_weight_offsets, dtype="fp32"):

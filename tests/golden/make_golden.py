@@ -141,6 +141,29 @@ def gen_gemm(K, torch):
     np.savez_compressed(OUT / "gemm.npz", **{f"{c}__{k}": v for c, d in cases.items() for k, v in d.items()})
 
 
+def gen_swiglu(K, torch):
+    """The reference's swiglu up projection (forward only: its backward is a
+    placeholder).  w1 holds each expert's gate block then its up block."""
+    cases = {}
+    g = torch.Generator().manual_seed(13)
+    for name, H, widths, counts in [("variable", 48, [64, 32, 48], [64, 32, 48]),
+                                    ("uniform", 32, [32, 32], [48, 0])]:
+        tok_off = torch.tensor([0] + list(np.cumsum(counts)), dtype=torch.int32)
+        w_off = torch.tensor([0] + list(np.cumsum([2 * w for w in widths])), dtype=torch.int32)
+        widths_t = torch.tensor(widths, dtype=torch.int32)
+        tpe = torch.tensor(counts, dtype=torch.int32)
+        P, TW, maxw = int(tok_off[-1]), int(w_off[-1]), max(widths)
+        x = torch.randn(P, H, generator=g)
+        w1 = torch.randn(H, TW, generator=g) * 0.1
+        out, pre = K.grouped_gemm_up(x, w1, tok_off, w_off, widths_t, tpe, maxw,
+                                     activation="swiglu", save_pre_act=True)
+        cases[name] = dict(H=np.int64(H), widths=np.array(widths), counts=np.array(counts),
+                           tok_off=np32(tok_off), w_off=np32(w_off), x=np32(x), w1=np32(w1),
+                           out=np32(out), pre=np32(pre))
+    np.savez_compressed(OUT / "swiglu.npz",
+                        **{f"{c}__{k}": v for c, d in cases.items() for k, v in d.items()})
+
+
 def gen_layer(moe_mod, torch):
     """BASELINE config 1 (and a variable-width variant): full layer fwd + bwd."""
     from triton_moe import TritonMoEConfig, TritonMoEMLP
@@ -178,15 +201,19 @@ def gen_layer(moe_mod, torch):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="generate only these files (route permute gemm swiglu layer)")
     a = ap.parse_args()
     moe_mod, K, gg = load_reference(a.ref)
     import torch
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    gen_route(K, torch)
-    gen_permute(K, torch)
-    gen_gemm(K, torch)
-    gen_layer(moe_mod, torch)
+    gens = {"route": lambda: gen_route(K, torch), "permute": lambda: gen_permute(K, torch),
+            "gemm": lambda: gen_gemm(K, torch), "swiglu": lambda: gen_swiglu(K, torch),
+            "layer": lambda: gen_layer(moe_mod, torch)}
+    for name, fn in gens.items():
+        if a.only is None or name in a.only:
+            fn()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

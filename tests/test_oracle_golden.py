@@ -90,6 +90,39 @@ def test_layer_forward_backward_matches_reference(case):
     close(res["dw2"], d["dw2"], "dw2")
 
 
+SWIGLU = load("swiglu")
+
+
+@pytest.mark.parametrize("case", sorted(SWIGLU))
+def test_swiglu_forward_matches_reference(case):
+    """The oracle's swiglu up projection reproduces the reference kernel's
+    (run under the Triton interpreter): output silu(gate) * up, pre_act = gate."""
+    d = SWIGLU[case]
+    maxw = int(d["widths"].max())
+    out, pre = orc.grouped_gemm_up(d["x"], d["w1"], d["tok_off"], d["w_off"], maxw, "swiglu")
+    scale = max(np.abs(d["out"]).max(), 1e-30)
+    np.testing.assert_allclose(out, d["out"], rtol=1e-5, atol=1e-5 * scale)
+    np.testing.assert_allclose(pre, d["pre"], rtol=1e-5, atol=1e-5 * max(np.abs(d["pre"]).max(), 1e-30))
+
+
+def test_swiglu_backward_is_the_gradient():
+    """The oracle's swiglu backward equals central differences of silu(g) * u."""
+    rng = np.random.default_rng(0)
+    g0 = rng.standard_normal((16, 32)).astype(np.float64)
+    u0 = rng.standard_normal((16, 32)).astype(np.float64)
+    go = rng.standard_normal((16, 32)).astype(np.float64)
+    f = lambda g, u: (g / (1 + np.exp(-g)) * u * go).sum()  # noqa: E731
+    ga = orc.swiglu_backward(go, g0, u0, [0, 16], [0, 64])
+    eps = 1e-4
+    for (i, j) in [(0, 0), (3, 7), (15, 31)]:
+        dg = np.zeros_like(g0); dg[i, j] = eps
+        du = np.zeros_like(u0); du[i, j] = eps
+        num_g = (f(g0 + dg, u0) - f(g0 - dg, u0)) / (2 * eps)
+        num_u = (f(g0, u0 + du) - f(g0, u0 - du)) / (2 * eps)
+        np.testing.assert_allclose(ga[i, j], num_g, rtol=1e-3, atol=1e-4)
+        np.testing.assert_allclose(ga[i, 32 + j], num_u, rtol=1e-3, atol=1e-4)
+
+
 def test_bf16_rounding_is_round_to_nearest_even():
     import torch
 

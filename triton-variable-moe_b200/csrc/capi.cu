@@ -33,6 +33,9 @@ int aux_finalize(const float* partials, int nblocks, int E, long long T, const i
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,
                 long long rows, const int32_t* rows_dev, const void* w, void* out, long long ldo,
                 int dtype, cudaStream_t st);
+int swiglu_grad(const void* g, const void* gate, const void* up, long long rows, long long ld,
+                const int32_t* tok_off, const int32_t* w_off, int E, void* out, long long ld_out,
+                int dtype, cudaStream_t st);
 int combine_rows(const void* y, long long ldy, int H, const int32_t* asg_row, long long T_tokens,
                  int k, const void* w, void* out, long long ldo, int dtype, cudaStream_t st);
 int relu2_grad(const void* g, const void* pre, long long rows, long long cols, long long ld,
@@ -273,6 +276,40 @@ Built build_up(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_
   return b;
 }
 
+// SwiGLU up projection: expert e's w1 columns are its gate block then its up
+// block (w_off spacing 2 w_e); out = silu(x @ gate) * (x @ up), gate / up
+// optionally stored (rounded) for the backward.
+Built build_up_swiglu(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_t hidden,
+                      int64_t total_width, const int32_t* tok_off, const int32_t* w_off,
+                      const int32_t* tpe, int E, void* out, void* gate, void* up, int64_t ld_out,
+                      int tile_n, int* status) {
+  if (!common_ok(rows, hidden, total_width, tok_off, w_off, E) || !x || !w1 || !out ||
+      ld_x < hidden || ld_out < 16 || ld_out % 8 != 0)
+    return bad(MOE_ERR_BAD_ARG);
+  Built b{};
+  b.g = base_desc(tok_off, tpe, w_off, E, hidden, status);
+  b.g.m_src = moe::DIM_TOKENS;
+  b.g.n_src = moe::DIM_HALF_WIDTH;
+  b.g.k_src = moe::DIM_CONST;
+  b.g.a_m_base = moe::BASE_TOK;
+  b.g.b_n_base = moe::BASE_WOFF;
+  b.g.d_m_base = moe::BASE_TOK;
+  b.g.d = out;
+  b.g.ldd = ld_out;
+  b.g.d_rows = rows;
+  b.g.aux = gate;
+  b.g.ld_aux = ld_out;
+  b.g.aux_rows = rows;
+  b.g.aux2 = up;
+  b.g.ld_aux2 = ld_out;
+  b.g.aux2_rows = rows;
+  b.epi = moe::EPI_SWIGLU;
+  b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
+                      pick_bn(tile_n, 0), 0};
+  b.op.pair = 1;
+  return b;
+}
+
 Built build_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
                  int64_t hidden, int64_t total_width, const int32_t* tok_off,
                  const int32_t* w_off, const int32_t* tpe, int E, void* out, int64_t ld_out,
@@ -432,6 +469,32 @@ int moe_grouped_gemm_up(const void* x, int64_t rows, int64_t ld_x, const void* w
                        expert_weight_offsets, tokens_per_expert, num_experts, activation, out,
                        pre_act, ld_out, tile_n, status),
               dtype, stream);
+}
+
+int moe_grouped_gemm_up_swiglu(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                               int64_t hidden, int64_t total_width,
+                               const int32_t* expert_token_offsets,
+                               const int32_t* expert_weight_offsets,
+                               const int32_t* tokens_per_expert, int num_experts, void* out,
+                               void* gate, void* up, int64_t ld_out, int dtype, int tile_n,
+                               int* status, void* stream) {
+  return run1(build_up_swiglu(x, rows, ld_x, w1, hidden, total_width, expert_token_offsets,
+                              expert_weight_offsets, tokens_per_expert, num_experts, out, gate,
+                              up, ld_out, tile_n, status),
+              dtype, stream);
+}
+
+int moe_swiglu_grad(const void* grad_out, const void* gate, const void* up, int64_t rows,
+                    int64_t ld, const int32_t* expert_token_offsets,
+                    const int32_t* expert_weight_offsets, int num_experts, void* grad_act,
+                    int64_t ld_act, int dtype, void* stream) {
+  if (rows < 0 || ld < 1 || ld_act < 1 || num_experts < 1 || num_experts > moe::kMaxGroups)
+    return MOE_ERR_BAD_ARG;
+  if (rows > 0 && (!grad_out || !gate || !up || !grad_act || !expert_token_offsets ||
+                   !expert_weight_offsets))
+    return MOE_ERR_BAD_ARG;
+  return moe::swiglu_grad(grad_out, gate, up, rows, ld, expert_token_offsets,
+                          expert_weight_offsets, num_experts, grad_act, ld_act, dtype, S(stream));
 }
 
 int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,

@@ -40,7 +40,8 @@ constexpr int kBarBytes = 512;            // mbarriers, TMEM address, abort flag
 struct Problem {
   GroupedGemmDesc g;
   int a_mn, b_mn, epi, bn;
-  int d_tma;  // tmD is valid: full slabs leave through TMA stores
+  int tile_n;  // output columns per tile: bn, or bn / 2 for SwiGLU (gate + up halves)
+  int d_tma;   // tmD is valid: full slabs leave through TMA stores
 };
 
 struct MultiParams {
@@ -48,6 +49,7 @@ struct MultiParams {
   CUtensorMap tmB[kMaxProblems];
   CUtensorMap tmD[kMaxProblems];  // epilogue output, 32-row x 128-byte boxes
   CUtensorMap tmX[kMaxProblems];  // epilogue aux (pre-activation), same boxes
+  CUtensorMap tmY[kMaxProblems];  // epilogue aux2 (SwiGLU up), same boxes
   Problem pr[kMaxProblems];
   int nprob;
   int stages;       // stages in the ring (depends on the largest N tile)
@@ -73,6 +75,7 @@ __device__ __forceinline__ int slot_base(int src, const Table& tb, int slot) {
 __device__ __forceinline__ int dim_value(int src, int e, const GroupedGemmDesc& g) {
   if (src == DIM_TOKENS) return g.tok_off[e + 1] - g.tok_off[e];
   if (src == DIM_WIDTH) return g.w_off[e + 1] - g.w_off[e];
+  if (src == DIM_HALF_WIDTH) return (g.w_off[e + 1] - g.w_off[e]) / 2;
   return g.cdim;
 }
 __device__ __forceinline__ int base_value(int src, int e, const GroupedGemmDesc& g) {
@@ -175,7 +178,7 @@ __device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& 
   r.p = lo < P.pr[0].g.E ? 0 : 1;  // slots are problem 0's experts, then problem 1's
   r.e = lo - (r.p ? P.pr[0].g.E : 0);
   r.slot = lo;
-  const int bn = P.pr[r.p].bn;
+  const int bn = P.pr[r.p].tile_n;
   const int local = t - tb.prefix[lo];
   const int ntn = (tb.N[lo] + bn - 1) / bn;
   r.m0 = (local / ntn) * BMT;
@@ -184,8 +187,12 @@ __device__ __forceinline__ Tile decode_tile(const Table& tb, const MultiParams& 
 }
 
 // Compile-time operand configuration of a problem slot: bit 0 = A MN-major,
-// bit 1 = B MN-major, bit 2 = N tile 256 (else 128).
-constexpr int cfg_of(int a_mn, int b_mn, int bn) { return a_mn | (b_mn << 1) | ((bn == 256) << 2); }
+// bit 1 = B MN-major, bit 2 = N tile 256 (else 128), bit 4 = the SwiGLU
+// epilogue is compiled in (only the up projection's kernels carry it).
+constexpr int kCfgSwiglu = 16;
+constexpr int cfg_of(int a_mn, int b_mn, int bn, bool swiglu = false) {
+  return a_mn | (b_mn << 1) | ((bn == 256) << 2) | (swiglu ? kCfgSwiglu : 0);
+}
 
 // Producer side of one tile: stream its k-blocks into the smem ring.  A tile
 // is 128 rows (A) / NT rows (B) of one 128-byte swizzle row of K each; an
@@ -197,7 +204,7 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
                                              uint64_t* empty, volatile int* abort_flag,
                                              const void* tA, const void* tB, int nkb, int am,
                                              int ak, int bn, int bk, int& stage,
-                                             uint32_t& phase) {
+                                             uint32_t& phase, int up_shift) {
   constexpr bool A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = ((CFG & 4) ? 256 : 128) / CG;  // B rows this CTA loads
   constexpr int BKE = Elem<T>::BKE;
@@ -216,9 +223,12 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
       tma_load_2d(a_dst, tA, &full[stage], ak + kc, am);
     }
     if constexpr (B_MN) {
+      // SwiGLU (up_shift != 0): the second half of the tile's columns comes
+      // from the expert's up block, up_shift columns further
 #pragma unroll
       for (int j = 0; j < NT / BKE; ++j)
-        tma_load_2d(b_dst + j * BKE * 128, tB, &full[stage], bn + BKE * j, bk + kc);
+        tma_load_2d(b_dst + j * BKE * 128, tB, &full[stage],
+                    bn + BKE * j + (j >= NT / BKE / 2 ? up_shift : 0), bk + kc);
     } else {
       tma_load_2d(b_dst, tB, &full[stage], bk + kc, bn);
     }
@@ -382,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (base_value(g.b_k_base, e, g) % kAlign) != 0 ||
                          (base_value(g.d_n_base, e, g) % kAlign) != 0;
         if (bad && g.status != nullptr) atomicExch(g.status, kStatusBadArg);
-        const int bn = P.pr[p].bn;
+        const int bn = P.pr[p].tile_n;
         tiles = (!bad && M > 0 && N > 0) ? ((M + BMT - 1) / BMT) * ((N + bn - 1) / bn) : 0;
       }
       tb.M[s] = M;
@@ -433,12 +443,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bn = slot_base(g.b_n_base, tb, tl.slot) + tl.n0 +
                        static_cast<int>(rank) * (pr.bn / CG);
         const int bk = slot_base(g.b_k_base, tb, tl.slot);
+        // SwiGLU: gate columns n0.. then up columns N + n0.. of the expert
+        const int up_shift = pr.epi == EPI_SWIGLU ? tb.N[tl.slot] - pr.bn / 2 : 0;
         if (tl.p == 0)
           ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0],
-                                         &P.tmB[0], nkb, am, ak, bn, bk, stage, phase);
+                                         &P.tmB[0], nkb, am, ak, bn, bk, stage, phase, up_shift);
         else
           ok = produce_tile<CFG1, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1],
-                                         &P.tmB[1], nkb, am, ak, bn, bk, stage, phase);
+                                         &P.tmB[1], nkb, am, ak, bn, bk, stage, phase, up_shift);
       }
     }
     __syncwarp();
@@ -548,11 +560,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const CUtensorMap* tmX = &P.tmX[tl.p];
       T* D = reinterpret_cast<T*>(g.d);
       T* AUX = reinterpret_cast<T*>(g.aux);
+      T* AUX2 = reinterpret_cast<T*>(g.aux2);
       const int rbase = tl.m0 + static_cast<int>(rank) * BM + q * 32;  // this warp's first row
       const int rows_ok = min(32, M - rbase);  // may be <= 0
       const long long grow0 = static_cast<long long>(slot_base(g.d_m_base, tb, slot)) + rbase;
       const int gcol0 = slot_base(g.d_n_base, tb, slot) + tl.n0;
-      const int ncols = min(pr.bn, N - tl.n0);
+      const int ncols = min(pr.tile_n, N - tl.n0);
       // fetch an aux (pre-activation) slab into staging slab `b` (lane 0)
       auto fetch_aux = [&](int b, int s) {
         fence_proxy_async_smem();  // the lanes' reads of the slab precede the load
@@ -609,6 +622,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int s = 0; s < ncols && rows_ok > 0; s += SLAB) {
         const int cvalid = min(SLAB, ncols - s);
+        if constexpr (((CFG0 | CFG1) & kCfgSwiglu) != 0) if (epi == EPI_SWIGLU) {
+          // gate accumulator columns at tbase + s, up columns tile_n further
+          const uint32_t tg = tbase + s, tu = tbase + pr.tile_n + s;
+          auto stage_cols = [&](uint32_t tcol, T* dst, const CUtensorMap* tm, long long ld) {
+            float v[SLAB];
+            if (K > 0) {
+              tmem_ld32(tcol, *reinterpret_cast<float(*)[32]>(&v[0]));
+              if constexpr (SLAB > 32)
+                if (cvalid > 32) tmem_ld32(tcol + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < SLAB; ++i) v[i] = 0.f;
+            }
+            uint8_t* stg = next_stage();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) *chunk_at(stg, lane, j) = pack_chunk<T>(&v[j * EPC]);
+            put(stg, tm, dst, ld, s, cvalid);
+          };
+          if (AUX != nullptr) stage_cols(tg, AUX, tmX, g.ld_aux);     // gate
+          if (AUX2 != nullptr) stage_cols(tu, AUX2, &P.tmY[tl.p], g.ld_aux2);  // up
+          // out = silu(gate) * up from the fp32 accumulators, 32 columns at a time
+          uint8_t* stg = next_stage();
+#pragma unroll
+          for (int h = 0; h < SLAB / 32; ++h) {
+            float gv[32], uv[32], o[32];
+            if (K > 0) {
+              tmem_ld32(tg + 32 * h, gv);
+              tmem_ld32(tu + 32 * h, uv);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) gv[i] = uv[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
+#pragma unroll
+            for (int j = 0; j < 32 / EPC; ++j)
+              *chunk_at(stg, lane, h * (32 / EPC) + j) = pack_chunk<T>(&o[j * EPC]);
+          }
+          put(stg, tmD, D, g.ldd, s, cvalid);
+          continue;
+        }
         float v[SLAB];
         if (K > 0) {
           tmem_ld32(tbase + s, *reinterpret_cast<float(*)[32]>(&v[0]));
@@ -793,14 +847,18 @@ int launch_single(int c, const MultiParams& P, int grid, cudaStream_t st) {
     case 4: return launch<T, 4, 4, CG>(P, grid, st);
     case 5: return launch<T, 5, 5, CG>(P, grid, st);
     case 6: return launch<T, 6, 6, CG>(P, grid, st);
-    default: return launch<T, 7, 7, CG>(P, grid, st);
+    case 7: return launch<T, 7, 7, CG>(P, grid, st);
+    // SwiGLU up projection (A K-major, B MN-major)
+    case kCfgSwiglu | 2: return launch<T, kCfgSwiglu | 2, kCfgSwiglu | 2, CG>(P, grid, st);
+    case kCfgSwiglu | 6: return launch<T, kCfgSwiglu | 6, kCfgSwiglu | 6, CG>(P, grid, st);
+    default: return kStatusUnsupported;
   }
 }
 // Two problems: a K-major/K-major problem followed by an MN-major/MN-major one
 // (the backward pairs), any N tiles.  Returns kStatusUnsupported otherwise.
 template <typename T, int CG>
 int launch_pair(int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
-  if ((c0 & 3) != 0 || (c1 & 3) != 3) return kStatusUnsupported;
+  if ((c0 & 3) != 0 || (c1 & 3) != 3 || ((c0 | c1) & kCfgSwiglu)) return kStatusUnsupported;
   const int k = ((c0 >> 2) & 1) | (((c1 >> 2) & 1) << 1);
   switch (k) {
     case 0: return launch<T, 0, 3, CG>(P, grid, st);
@@ -864,7 +922,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   // CTA pairs (256-row tiles) only when every problem of the launch asks
   int cg = 2;
   for (int i = 0; i < n; ++i)
-    if (gs[i].E != 0 && ops[i].pair != 2) cg = 1;
+    if (gs[i].E != 0 && (ops[i].pair != 2 || epis[i] == EPI_SWIGLU)) cg = 1;
   for (int i = 0; i < n; ++i) {
     const GemmOperands& op = ops[i];
     const GroupedGemmDesc& g = gs[i];
@@ -895,13 +953,20 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
                                         g.ld_aux, bke, 32, false)
                             : kStatusBadArg;
       if (epis[i] == EPI_DACT && sx != kStatusOk) return kStatusBadArg;
-      P.pr[used].d_tma = (sd == kStatusOk && sx == kStatusOk) ? 1 : 0;
+      int sy = kStatusOk;
+      if (g.aux2 != nullptr && epis[i] == EPI_SWIGLU)
+        sy = g.aux2_rows > 0 ? make_tmap(&P.tmY[used], g.aux2, dtype, g.ld_aux2, g.aux2_rows,
+                                         g.ld_aux2, bke, 32, false)
+                             : kStatusBadArg;
+      P.pr[used].d_tma = (sd == kStatusOk && sx == kStatusOk && sy == kStatusOk) ? 1 : 0;
     }
     P.pr[used].g = g;
     P.pr[used].a_mn = op.a_mn;
     P.pr[used].b_mn = op.b_mn;
     P.pr[used].epi = epis[i];
     P.pr[used].bn = bn;
+    P.pr[used].tile_n = epis[i] == EPI_SWIGLU ? bn / 2 : bn;
+    if (epis[i] == EPI_SWIGLU && !op.b_mn) return kStatusUnsupported;  // gate/up boxes along N
     bn_max = bn > bn_max ? bn : bn_max;
     if (op.grid > grid) grid = op.grid;
     ++used;
@@ -910,8 +975,10 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   P.nprob = used;
   if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0) grid = num_sms();
-  const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn);
-  const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn) : c0;
+  const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn, P.pr[0].epi == EPI_SWIGLU);
+  const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn,
+                                   P.pr[1].epi == EPI_SWIGLU)
+                          : c0;
   int rc = dispatch_dtype(dtype, cg, used, c0, c1, P, grid, st);
   if (rc != kStatusUnsupported) return rc;
   // no compiled pair for these configurations: one launch per problem
@@ -922,9 +989,10 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
     Q.tmB[0] = P.tmB[i];
     Q.tmD[0] = P.tmD[i];
     Q.tmX[0] = P.tmX[i];
+    Q.tmY[0] = P.tmY[i];
     Q.pr[0] = P.pr[i];
     if (!plan_smem(Q, P.pr[i].bn, cg)) return kStatusUnsupported;
-    const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn);
+    const int ci = cfg_of(Q.pr[0].a_mn, Q.pr[0].b_mn, Q.pr[0].bn, Q.pr[0].epi == EPI_SWIGLU);
     rc = dispatch_dtype(dtype, cg, 1, ci, ci, Q, grid, st);
     if (rc != kStatusOk) return rc;
   }

@@ -22,6 +22,7 @@ enum DimSrc : int {
   DIM_CONST = 0,   // a constant (the hidden size)
   DIM_TOKENS = 1,  // token rows of the expert: off[e+1] - off[e]
   DIM_WIDTH = 2,   // expert width: woff[e+1] - woff[e]
+  DIM_HALF_WIDTH = 3,  // (woff[e+1] - woff[e]) / 2: SwiGLU, gate and up columns per expert
 };
 // Where a per-expert coordinate base comes from.
 enum BaseSrc : int {
@@ -34,6 +35,8 @@ enum EpiMode : int {
   EPI_STORE = 0,  // D = acc
   EPI_RELU2 = 1,  // aux = relu(acc); D = relu(acc)^2  (both rounded from fp32)
   EPI_DACT = 2,   // g = round(acc); D = pre > 0 ? g * 2 * pre : 0, pre read from aux
+  EPI_SWIGLU = 3,  // the tile's B holds gate columns then up columns:
+                   // D = silu(gate) * up; aux = gate, aux2 = up (both optional)
 };
 
 constexpr int kMaxGroups = 256;
@@ -55,6 +58,9 @@ struct GroupedGemmDesc {
   void* aux;
   long long ld_aux;
   long long aux_rows;  // rows of the aux allocation
+  void* aux2;  // second epilogue output (SwiGLU: up), ld_aux2, aux2_rows rows
+  long long ld_aux2;
+  long long aux2_rows;
   int* status;  // device status word: set non-zero when a wait gave up
 };
 

@@ -297,6 +297,43 @@ __global__ void relu2_grad_kernel(const T* __restrict__ g, const T* __restrict__
   }
 }
 
+// SwiGLU backward, elementwise over [rows, w_e] per expert: from the output
+// gradient g and the saved gate / up values,
+//   s = sigmoid(gate), dgate = g * up * s * (1 + gate * (1 - s)), dup = g * gate * s,
+// written (rounded) into grad_act[r, 0:w_e) and [w_e, 2 w_e) — the gate/up column
+// layout of w1 — so the dX / dW GEMMs run over width 2 w_e.  One warp per row;
+// the row's expert comes from a binary search over the token offsets.
+template <typename T>
+__global__ void swiglu_grad_kernel(const T* __restrict__ g, const T* __restrict__ gate,
+                                   const T* __restrict__ up, long long rows, long long ld,
+                                   const int32_t* __restrict__ tok_off,
+                                   const int32_t* __restrict__ w_off, int E,
+                                   T* __restrict__ out, long long ld_out) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long end = min(rows, static_cast<long long>(tok_off[E]));
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < end; r += warps) {
+    int lo = 0, hi = E - 1;  // last expert whose first row is <= r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tok_off[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int w = (w_off[lo + 1] - w_off[lo]) / 2;
+    for (int c = lane; c < w; c += 32) {
+      const float gv = V8<T>::to_f(g[r * ld + c]);
+      const float a = V8<T>::to_f(gate[r * ld + c]);
+      const float u = V8<T>::to_f(up[r * ld + c]);
+      const float sg = 1.0f / (1.0f + expf(-a));
+      out[r * ld_out + c] = V8<T>::from_f(gv * u * sg * (1.0f + a * (1.0f - sg)));
+      out[r * ld_out + w + c] = V8<T>::from_f(gv * a * sg);
+    }
+  }
+  pdl_done();
+}
+
 // Sorted-order metadata -> padded row maps (row_asg pre-filled with -1).
 __global__ void build_row_map_kernel(const int32_t* __restrict__ indices,
                                      const int32_t* __restrict__ bin_ids,
@@ -404,6 +441,22 @@ int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long 
 
 
 }  // namespace
+
+int swiglu_grad(const void* g, const void* gate, const void* up, long long rows, long long ld,
+                const int32_t* tok_off, const int32_t* w_off, int E, void* out, long long ld_out,
+                int dtype, cudaStream_t st) {
+  if (rows <= 0) return kStatusOk;
+  const int grid = grid_for(rows, kThreadsPerBlock / 32);
+#define MOE_SWIGLU(T)                                                                        \
+  return launch_pdl(swiglu_grad_kernel<T>, grid, st, static_cast<const T*>(g),               \
+                    static_cast<const T*>(gate), static_cast<const T*>(up), rows, ld, tok_off, \
+                    w_off, E, static_cast<T*>(out), ld_out)
+  if (dtype == 0) MOE_SWIGLU(__nv_bfloat16);
+  if (dtype == 1) MOE_SWIGLU(__half);
+  if (dtype == 2) MOE_SWIGLU(float);
+#undef MOE_SWIGLU
+  return kStatusUnsupported;
+}
 
 // dtype: 0 bf16, 1 fp16, 2 fp32
 int gather_rows(const void* x, long long ldx, int H, const int32_t* map, int div,

@@ -28,7 +28,7 @@ STATUS_TEXT = {
 }
 
 DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
-ACT_CODE = {"none": 0, "relu_squared": 1}
+ACT_CODE = {"none": 0, "relu_squared": 1, "swiglu": 2}
 ROUND_CODE = {"up": 0, "down": 1, "nearest": 2}
 TILE_PAIR = 0x200  # tile_n flag: 256-row tiles on SM pairs (2-CTA clusters)
 
@@ -55,6 +55,9 @@ _SIGS = {
     "moe_padded_scatter": [_P, _L, _L, _P, _L, _I, _P, _P, _L, _I, _P],
     "moe_relu_squared_grad": [_P, _P, _L, _L, _L, _P, _I, _P],
     "moe_grouped_gemm_up": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _I, _P, _P, _L, _I, _I, _P, _P],
+    "moe_grouped_gemm_up_swiglu": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _P, _P, _L, _I, _I,
+                                   _P, _P],
+    "moe_swiglu_grad": [_P, _P, _P, _L, _L, _P, _P, _I, _P, _L, _I, _P],
     "moe_grouped_gemm_down": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _I, _I, _P, _P],
     "moe_grouped_gemm_up_dx": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _I, _I, _P, _P],
     "moe_grouped_gemm_up_dw": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _I, _P, _I, _I, _P, _P],

@@ -385,6 +385,42 @@ def gemm_up(x, w1, tok_off, w_off, tok_cnt, num_experts, activation, out, pre_ac
     return out
 
 
+def gemm_up_swiglu(x, w1, tok_off, w_off, tok_cnt, num_experts, out, gate=None, up=None,
+                   tile_n=0):
+    """out = silu(x @ gate_e) * (x @ up_e) per expert (w1 columns: gate block then
+    up block per expert, w_off stepping by 2 w_e); gate / up optionally stored."""
+    _gemm_check(x, w1, out)
+    for t in (gate, up):
+        if t is not None and (t.stride(0) != out.stride(0) or t.dtype != out.dtype):
+            raise ValueError("gate / up must match out's dtype and row stride")
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    H, TW = w1.shape
+    ev = _ev_begin()
+    rc = lib.moe_grouped_gemm_up_swiglu(
+        ptr(x), x.shape[0], x.stride(0), ptr(w1), H, TW, ptr(tok_off), ptr(w_off), ptr(tok_cnt),
+        int(num_experts), ptr(out), ptr(gate), ptr(up), out.stride(0), DTYPE_CODE[x.dtype],
+        int(tile_n), ptr(status_buffer(x.device)), stream_handle(x.device),
+    )
+    _ev_end(ev, "grouped_gemm_up")
+    check(rc, "moe_grouped_gemm_up_swiglu")
+    _count(1)
+    return out
+
+
+def swiglu_grad(grad_out, gate, up, tok_off, w_off, num_experts, out):
+    """[dgate | dup] per expert in w1's gate/up column layout (out: [rows, >= 2 max_w])."""
+    require_cuda(grad_out, gate, up, out)
+    if not (grad_out.stride(0) == gate.stride(0) == up.stride(0)):
+        raise ValueError("grad_out, gate and up must share a row stride")
+    rc = lib.moe_swiglu_grad(ptr(grad_out), ptr(gate), ptr(up), grad_out.shape[0],
+                             grad_out.stride(0), ptr(_meta(tok_off)), ptr(_meta(w_off)),
+                             int(num_experts), ptr(out), out.stride(0),
+                             DTYPE_CODE[grad_out.dtype], stream_handle(grad_out.device))
+    check(rc, "moe_swiglu_grad")
+    _count(1)
+    return out
+
+
 def gemm_down(inter, w2, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0):
     _gemm_check(inter, w2, out)
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)

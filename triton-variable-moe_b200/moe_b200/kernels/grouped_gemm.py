@@ -17,10 +17,15 @@ Layouts (as in the reference):
     intermediate: [total_tokens, max_expert_width]; expert e uses columns
         [0, w_e) of its rows, the other columns are zero.
 
-Activations: "relu_squared" and "none" are supported.  The reference's
-"swiglu" backward is an acknowledged placeholder (grouped_gemm.py:768-789,
-930-942), so there is no result to match and "swiglu" raises
-NotImplementedError here.
+Activations: "relu_squared", "none" and "swiglu".  For "swiglu" expert e's
+w1 columns are its gate block then its up block (expert_weight_offsets step by
+2 w_e, the reference's layout, grouped_gemm.py:296-358); the forward matches
+the reference's (output silu(gate) * up, pre_act = gate).  The reference's
+swiglu backward is an acknowledged placeholder (grouped_gemm.py:768-789,
+930-942); here it is the true gradient: dgate = g * up * silu'(gate),
+dup = g * silu(gate), then the usual dX / dW GEMMs over width 2 w_e.  The up
+projection is kept by the autograd function, or recomputed when
+grouped_gemm_up_backward is called without it.
 """
 
 from __future__ import annotations
@@ -31,7 +36,16 @@ from torch.autograd.function import once_differentiable
 
 from . import _ops
 
-_SUPPORTED_ACTIVATIONS = ("relu_squared", "none")
+_SUPPORTED_ACTIVATIONS = ("relu_squared", "none", "swiglu")
+
+
+def _check_swiglu_layout(expert_weight_offsets, expert_widths) -> None:
+    """The swiglu kernels take each expert's up block right after its gate block."""
+    off = expert_weight_offsets.to(torch.int64)
+    wid = expert_widths.to(torch.int64)
+    if not torch.equal(off[1:] - off[:-1], 2 * wid):
+        raise ValueError("swiglu: expert_weight_offsets must step by 2 * expert_widths "
+                         "(each expert's gate columns, then its up columns)")
 
 
 def _check_activation(activation: str) -> None:
@@ -90,6 +104,14 @@ def grouped_gemm_up(
     pre = torch.zeros_like(out) if save_pre_act else None
     if total_tokens == 0:
         return (out, pre) if save_pre_act else out
+    if activation == "swiglu":
+        _check_swiglu_layout(expert_weight_offsets, expert_widths)
+        if gather_map is not None:
+            x = _gather_rows(x, gather_map, total_tokens)
+        _ops.gemm_up_swiglu(x.contiguous(), w1.contiguous(), expert_token_offsets,
+                            expert_weight_offsets, tokens_per_expert, len(expert_widths), out,
+                            gate=pre)
+        return (out, pre) if save_pre_act else out
     if gather_map is not None:
         x = _gather_rows(x, gather_map, total_tokens)
     _ops.gemm_up(x.contiguous(), w1.contiguous(), expert_token_offsets, expert_weight_offsets,
@@ -134,8 +156,12 @@ def grouped_gemm_up_backward(
     hidden_size: int,
     activation: str = "relu_squared",
     gather_map: torch.Tensor | None = None,
+    up_act: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Gradients of grouped_gemm_up: (grad_x in gathered space, grad_w1)."""
+    """Gradients of grouped_gemm_up: (grad_x in gathered space, grad_w1).
+
+    For "swiglu", pre_act is the gate projection and up_act the up projection
+    (recomputed when not given)."""
     _check_activation(activation)
     total_tokens = int(expert_token_offsets[-1].item())
     dtype = x.dtype
@@ -144,12 +170,25 @@ def grouped_gemm_up_backward(
     if total_tokens == 0:
         return grad_x, grad_w1
     g = grad_output.to(dtype).contiguous()
+    E = len(expert_widths)
+    xs = _gather_rows(x, gather_map, total_tokens) if gather_map is not None else x.contiguous()
+    if activation == "swiglu":
+        _check_swiglu_layout(expert_weight_offsets, expert_widths)
+        gate = pre_act.to(dtype).contiguous()
+        if up_act is None:  # recompute the up projection
+            up_act = torch.zeros_like(gate)
+            _ops.gemm_up_swiglu(xs, w1.contiguous(), expert_token_offsets, expert_weight_offsets,
+                                tokens_per_expert, E, torch.empty_like(gate), up=up_act)
+        up = up_act.to(dtype).contiguous()
+        grad_act = torch.zeros(total_tokens, 2 * gate.shape[1], device=x.device, dtype=dtype)
+        _ops.swiglu_grad(g, gate, up, expert_token_offsets, expert_weight_offsets, E, grad_act)
+        _ops.gemm_up_backward(grad_act, xs, w1.contiguous(), expert_token_offsets,
+                              expert_weight_offsets, tokens_per_expert, E, grad_x, grad_w1)
+        return grad_x, grad_w1
     if activation == "relu_squared":
         grad_act = _ops.relu_squared_grad(g, pre_act)
     else:
         grad_act = g
-    E = len(expert_widths)
-    xs = _gather_rows(x, gather_map, total_tokens) if gather_map is not None else x.contiguous()
     _ops.gemm_up_backward(grad_act, xs, w1.contiguous(), expert_token_offsets, expert_weight_offsets,
                           tokens_per_expert, E, grad_x, grad_w1)
     return grad_x, grad_w1
@@ -193,14 +232,28 @@ class GroupedGemmUp(torch.autograd.Function):
     def forward(ctx, x, w1, expert_token_offsets, expert_weight_offsets, expert_widths,
                 tokens_per_expert, max_expert_width, hidden_size, activation, x_flat, gather_map):
         x = x.to(w1.dtype)
-        output, pre_act = grouped_gemm_up(x, w1, expert_token_offsets, expert_weight_offsets,
-                                          expert_widths, tokens_per_expert, max_expert_width,
-                                          activation=activation, save_pre_act=True)
+        up_act = None
+        if activation == "swiglu":
+            # keep the up projection too (the backward needs gate and up)
+            _check_activation(activation)
+            _check_swiglu_layout(expert_weight_offsets, expert_widths)
+            total_tokens = int(expert_token_offsets[-1].item())
+            output = torch.zeros(total_tokens, max_expert_width, device=x.device, dtype=x.dtype)
+            pre_act = torch.zeros_like(output)
+            up_act = torch.zeros_like(output)
+            if total_tokens > 0:
+                _ops.gemm_up_swiglu(x.contiguous(), w1.contiguous(), expert_token_offsets,
+                                    expert_weight_offsets, tokens_per_expert, len(expert_widths),
+                                    output, gate=pre_act, up=up_act)
+        else:
+            output, pre_act = grouped_gemm_up(x, w1, expert_token_offsets, expert_weight_offsets,
+                                              expert_widths, tokens_per_expert, max_expert_width,
+                                              activation=activation, save_pre_act=True)
         ctx.use_gather_map = x_flat is not None and gather_map is not None
         x_saved = x_flat.to(w1.dtype) if ctx.use_gather_map else x
         ctx.save_for_backward(x_saved, w1, pre_act, expert_token_offsets, expert_weight_offsets,
                               expert_widths, tokens_per_expert,
-                              gather_map if ctx.use_gather_map else None)
+                              gather_map if ctx.use_gather_map else None, up_act)
         ctx.max_expert_width = max_expert_width
         ctx.hidden_size = hidden_size
         ctx.activation = activation
@@ -210,10 +263,11 @@ class GroupedGemmUp(torch.autograd.Function):
     @custom_bwd(device_type="cuda")
     @once_differentiable
     def backward(ctx, grad_output):
-        (x_for_dw, w1, pre_act, tok_off, w_off, widths, tpe, gather_map) = ctx.saved_tensors
+        (x_for_dw, w1, pre_act, tok_off, w_off, widths, tpe, gather_map,
+         up_act) = ctx.saved_tensors
         grad_x, grad_w1 = grouped_gemm_up_backward(
             grad_output, x_for_dw, w1, pre_act, tok_off, w_off, widths, tpe, ctx.hidden_size,
-            ctx.activation, gather_map=gather_map,
+            ctx.activation, gather_map=gather_map, up_act=up_act,
         )
         return grad_x, grad_w1, None, None, None, None, None, None, None, None, None
 
