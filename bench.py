@@ -6,8 +6,7 @@
 A step is one training pass of the MoE layer over one synthetic batch:
 `out, aux, f_i = layer(x); out.backward(g)` (router, routing, gather, grouped
 GEMM up with relu^2, grouped GEMM down, weighted combine, and the full
-backward).  The default workload is BASELINE config 3, the north-star
-768-hidden variable-expert layer: n_embd=768, experts 4x512 + 8x256 + 4x128,
+backward).  The default workload (c3) is the 768-hidden variable-expert layer: n_embd=768, experts 4x512 + 8x256 + 4x128,
 top-2, batch 8 x seq 1024 = 8192 tokens, bf16, x ~ N(0,1), weights N(0,0.02),
 router from a random-init linear.
 
@@ -554,7 +553,7 @@ def run_b200(args, cfg, name):
 
     def e2e_run(n):
         comp = torch.cuda.current_stream()
-        up, down = torch.cuda.Stream(), torch.cuda.Stream()
+        up, up2, down = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
         ev = lambda: torch.cuda.Event()  # noqa: E731
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         in_ready = [ev() for _ in range(n)]
@@ -567,13 +566,20 @@ def run_b200(args, cfg, name):
         t0.record(comp)
 
         def upload(i):
+            # tokens and output gradient on two copy streams (two DMA engines)
             xs, gs = slots[i % 2][0], slots[i % 2][1]
-            up.wait_event(t0)
-            if i >= 2:
-                up.wait_event(computed[i - 2])  # the slot's previous step is done with it
-            with torch.cuda.stream(up), torch.no_grad():
-                xs.copy_(x_host, non_blocking=True)
-                gs.copy_(g_host, non_blocking=True)
+            for st in (up, up2):
+                st.wait_event(t0)
+                if i >= 2:
+                    st.wait_event(computed[i - 2])  # the slot's previous step is done with it
+            with torch.no_grad():
+                with torch.cuda.stream(up):
+                    xs.copy_(x_host, non_blocking=True)
+                with torch.cuda.stream(up2):
+                    gs.copy_(g_host, non_blocking=True)
+                    gs_done = torch.cuda.Event()
+                    gs_done.record(up2)
+                up.wait_event(gs_done)
                 in_ready[i].record(up)
 
         upload(0)
@@ -657,8 +663,9 @@ def run_b200(args, cfg, name):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nbytes,
                     "d2h_bytes_per_step": nbytes, "ms_per_step": e2e_ms / args.steps,
-                    "copies": "pinned host <-> device on two copy streams, overlapped with "
-                              "the neighbouring steps' compute (two device slots)",
+                    "copies": "pinned host -> device on two copy streams (tokens, output "
+                              "gradient) and device -> host on a third, overlapped with the "
+                              "neighbouring steps' compute (two device slots)",
                     "output_matches_device": e2e_ok},
             "gpu_launches": launches,
             "clocks": clocks,

@@ -165,7 +165,8 @@ def gen_swiglu(K, torch):
 
 
 def gen_layer(moe_mod, torch):
-    """BASELINE config 1 (and a variable-width variant): full layer fwd + bwd."""
+    """The small CPU config (n_embd 64, 4 experts x 128, top-2, 2 x 16 tokens) and a
+    variable-width variant: full layer fwd + bwd."""
     from triton_moe import TritonMoEConfig, TritonMoEMLP
 
     cases = {}

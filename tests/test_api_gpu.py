@@ -5,7 +5,7 @@ the CPU oracle.
   the golden vectors must be reproduced exactly (copies) or to fp32 rounding;
 * the same ops in bf16: bit-exact against the oracle's bf16 restatement;
 * the grouped GEMM API (up / down / both backwards, with and without the
-  fused-gather map) in bf16 on the golden inputs: within the north-star bound
+  fused-gather map) in bf16 on the golden inputs: within the bf16 bound
   |a - b| <= 1e-2 * scale + 2e-2 * |b| of the oracle run in fp32 on the same
   bf16-rounded inputs, where scale = max |b| of the tensor (the golden values
   are O(1e-1), so a bare 1e-2 absolute bound would be vacuous).

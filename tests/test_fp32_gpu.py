@@ -7,7 +7,7 @@ dots.  Checked against
   fp32 k-block; tolerance |a-b| <= 1e-2 * scale + 1e-2 |b| (tf32 keeps 10
   mantissa bits, so each product carries ~5e-4 relative error);
 * the reference's fp32 golden vectors for the whole layer (forward with its
-  own routing, and all gradients), under the north-star bound.
+  own routing, and all gradients), within |a - b| <= 1e-2 * scale + 2e-2 * |b|.
 """
 
 import math

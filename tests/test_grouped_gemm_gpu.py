@@ -4,7 +4,7 @@ Each of the six MoE GEMMs is checked expert by expert on random grouped
 problems, including experts with no rows, widths that are not multiples of
 the 64-wide k-block, both N tiles, and the fused relu^2 / relu^2-derivative
 epilogues.  Tolerance (bf16 storage, fp32 accumulation): |a-b| <= 1e-2 +
-2e-2 |b|, the bound BASELINE's north star states for bf16 results.
+2e-2 |b| (bf16 results against an fp32 reference).
 """
 
 import math

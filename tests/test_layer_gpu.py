@@ -2,9 +2,9 @@
 
 * Golden: the layer body driven with the reference run's own routing choice
   (selected experts + weights from the fp32 reference golden vectors) must
-  match the reference's fp32 outputs and gradients within the north-star
+  match the reference's fp32 outputs and gradients within the bf16
   bound |a - b| <= 1e-2 * scale + 2e-2 * |b| (bf16 storage vs fp32).
-* Oracle: at BASELINE's bf16 shapes (README uniform / variable, the 768-hidden
+* Oracle: at the benchmark bf16 shapes (README uniform / variable, the 768-hidden
   variable config) the module's output and gradients match the CPU oracle run
   on the module's own routing with the reference's bf16 rounding points.
 * Properties: determinism, dtypes/shapes, aux losses, state_dict layout.

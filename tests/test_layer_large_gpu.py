@@ -1,4 +1,4 @@
-"""The layer at BASELINE's large shapes (config 4: 2048 hidden, 64 experts,
+"""The layer at the large benchmark shapes (c4: 2048 hidden, 64 experts,
 top-8, Zipf-skewed routing; and a 4096-hidden, 128-expert variable layer at a
 reduced token count) against a plain PyTorch fp32 reference of the same
 routing, computed expert by expert on the GPU.  Tolerance (bf16 storage):

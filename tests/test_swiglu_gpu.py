@@ -3,7 +3,7 @@
 * Forward against the reference's own kernel (golden vectors made under the
   Triton interpreter, fp32) and the oracle in bf16: out = silu(gate) * up with
   each expert's w1 columns laid out gate block then up block, pre_act = gate.
-  Tolerance: the north-star bound |a - b| <= 1e-2 * max|b| + 2e-2 * |b|.
+  Tolerance: the bf16 bound |a - b| <= 1e-2 * max|b| + 2e-2 * |b|.
 * The stored gate / up projections against torch fp32, both N tiles, ragged
   widths (not multiples of the tile).
 * Backward: the reference's swiglu backward is a placeholder, so gradients are
