@@ -266,6 +266,25 @@ MOE_API int moe_swiglu_grad(const void* grad_out, const void* gate, const void* 
                             const int32_t* expert_weight_offsets, int num_experts,
                             void* grad_act, int64_t ld_act, int dtype, void* stream);
 
+/* grouped_gemm_up (relu^2, saving pre_act) and grouped_gemm_down in ONE
+ * persistent launch: inter = relu(x @ w1_e)^2, out = inter @ w2_e.  A down tile
+ * starts as soon as every up tile of its 128-row block has stored its rows (a
+ * per-block count in `dep`), so the down tiles fill the SMs the up tiles' tail
+ * leaves idle instead of waiting for a second launch.  dep: an int32 device
+ * buffer of at least moe_up_down_dep_words(rows, num_experts) words, zero
+ * before the first call; each call returns it to zero.  Calls sharing a dep
+ * buffer must not overlap. */
+MOE_API int64_t moe_up_down_dep_words(int64_t rows, int num_experts);
+MOE_API int moe_grouped_gemm_up_down(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                                     const void* w2, int64_t hidden, int64_t total_width,
+                                     const int32_t* expert_token_offsets,
+                                     const int32_t* expert_weight_offsets,
+                                     const int32_t* tokens_per_expert, int num_experts,
+                                     void* inter, void* pre_act, int64_t ld_inter, void* out,
+                                     int64_t ld_out, int32_t* dep, int64_t dep_words, int dtype,
+                                     int tile_n_width, int tile_n_hidden, int* status,
+                                     void* stream);
+
 /* grouped_gemm_down (grouped_gemm.py:586-651, kernel :480-583):
  * out[rows_e] = inter[rows_e, :w_e] @ w2[w_e rows]. */
 MOE_API int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,

@@ -256,3 +256,33 @@ def test_fused_backward_launches(case, pair, device):
         r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]
         ref = t["x"][r0:r1].float().T @ t["ga"][r0:r1, : c1 - c0].float()
         assert_close(gw1[:, c0:c1], ref, f"gw1 e{e}")
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+@pytest.mark.parametrize("tiles", [(128, 128), (256, 256), (128, 256)])
+def test_fused_up_down_matches_separate_launches(case, tiles, device):
+    """One launch of up (relu^2) + down with row-block dependencies gives exactly
+    the two separate launches' results, and leaves its counters at zero."""
+    from moe_b200.kernels import _ops
+
+    widths, counts, H, bs = case
+    t, m = make_problem(widths, counts, H, bs, device=device, seed=12)
+    args = (m["tok_off"], m["w_off"], m["tpe"], m["E"])
+    tw, th = tiles
+    for rep in range(3):  # the counters are reused across launches
+        h = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
+        pre = torch.zeros_like(h)
+        y = torch.zeros(m["rows"], H, dtype=torch.bfloat16, device=device)
+        _ops.gemm_up_down(t["x"], t["w1"], t["w2"], *args, h, pre, y, tile_n_width=tw,
+                          tile_n_hidden=th)
+        h2 = torch.zeros_like(h)
+        pre2 = torch.zeros_like(h)
+        _ops.gemm_up(t["x"], t["w1"], *args, "relu_squared", h2, pre2, tile_n=tw)
+        y2 = torch.zeros_like(y)
+        _ops.gemm_down(h2, t["w2"], *args, y2, tile_n=th)
+        torch.cuda.synchronize()
+        _ops.check_device_status(device)
+        assert torch.equal(h, h2) and torch.equal(pre, pre2)
+        assert torch.equal(y, y2)
+        dep = _ops.up_down_dep_buffer(device, m["rows"], m["E"])
+        assert int(dep.abs().sum().item()) == 0

@@ -497,6 +497,36 @@ int moe_swiglu_grad(const void* grad_out, const void* gate, const void* up, int6
                           expert_weight_offsets, num_experts, grad_act, ld_act, dtype, S(stream));
 }
 
+int64_t moe_up_down_dep_words(int64_t rows, int num_experts) {
+  if (rows < 0 || num_experts < 1) return 0;
+  return 2 * (rows / 128 + num_experts + 1);
+}
+
+int moe_grouped_gemm_up_down(const void* x, int64_t rows, int64_t ld_x, const void* w1,
+                             const void* w2, int64_t hidden, int64_t total_width,
+                             const int32_t* expert_token_offsets,
+                             const int32_t* expert_weight_offsets,
+                             const int32_t* tokens_per_expert, int num_experts, void* inter,
+                             void* pre_act, int64_t ld_inter, void* out, int64_t ld_out,
+                             int32_t* dep, int64_t dep_words, int dtype, int tile_n_width,
+                             int tile_n_hidden, int* status, void* stream) {
+  if (!dep || dep_words < moe_up_down_dep_words(rows, num_experts)) return MOE_ERR_BAD_ARG;
+  Built up = build_up(x, rows, ld_x, w1, hidden, total_width, expert_token_offsets,
+                      expert_weight_offsets, tokens_per_expert, num_experts,
+                      MOE_ACT_RELU_SQUARED, inter, pre_act, ld_inter, tile_n_width, status);
+  Built down = build_down(inter, rows, ld_inter, w2, hidden, total_width, expert_token_offsets,
+                          expert_weight_offsets, tokens_per_expert, num_experts, out, ld_out,
+                          tile_n_hidden, status);
+  const int half = static_cast<int>(dep_words / 2);
+  up.g.dep = dep;
+  up.g.dep_len = half;
+  up.g.dep_role = 1;
+  down.g.dep = dep;
+  down.g.dep_len = half;
+  down.g.dep_role = 2;
+  return run2(up, down, dtype, stream);
+}
+
 int moe_grouped_gemm_down(const void* inter, int64_t rows, int64_t ld_inter, const void* w2,
                           int64_t hidden, int64_t total_width,
                           const int32_t* expert_token_offsets,

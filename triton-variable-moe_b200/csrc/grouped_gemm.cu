@@ -63,8 +63,9 @@ struct MultiParams {
 struct Table {
   int* prefix;  // [nge + 1]
   int *M, *N, *K, *tok, *wof;  // [nge] each
+  int* mtp;  // [nge] first row block (of BMT rows) of each problem-0 slot
 };
-__host__ __device__ constexpr int table_bytes(int nge) { return (6 * nge + 1) * 4; }
+__host__ __device__ constexpr int table_bytes(int nge) { return (7 * nge + 1) * 4; }
 
 __device__ __forceinline__ int slot_base(int src, const Table& tb, int slot) {
   if (src == BASE_TOK) return tb.tok[slot];
@@ -327,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tb.K = tb.N + nge;
   tb.tok = tb.K + nge;
   tb.wof = tb.tok + nge;
+  tb.mtp = tb.wof + nge;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int per = (nge + 31) / 32;
     const int beg = lane * per;
     const int end = min(nge, beg + per);
-    int sum = 0;
+    int sum = 0, msum = 0;
     for (int s = beg; s < end; ++s) {
       const int p = s < P.pr[0].g.E ? 0 : 1;
       const int e = s - (p ? P.pr[0].g.E : 0);
@@ -400,17 +402,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tb.K[s] = K;
       tb.tok[s] = g.tok_off[e];
       tb.wof[s] = g.w_off[e];
-      tb.prefix[s] = sum;  // chunk-local exclusive prefix for now
+      tb.prefix[s] = sum;  // chunk-local exclusive prefixes for now
       sum += tiles;
+      tb.mtp[s] = msum;
+      if (p == 0) msum += (M + BMT - 1) / BMT;
     }
-    int incl = sum;
+    int incl = sum, mincl = msum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
+      const int mv = __shfl_up_sync(0xffffffffu, mincl, o);
+      if (lane >= o) {
+        incl += v;
+        mincl += mv;
+      }
     }
-    const int excl = incl - sum;
-    for (int s = beg; s < end; ++s) tb.prefix[s] += excl;
+    const int excl = incl - sum, mexcl = mincl - msum;
+    for (int s = beg; s < end; ++s) {
+      tb.prefix[s] += excl;
+      tb.mtp[s] += mexcl;
+    }
     if (lane == 31) tb.prefix[nge] = incl;
   }
   __syncthreads();
@@ -445,6 +456,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bk = slot_base(g.b_k_base, tb, tl.slot);
         // SwiGLU: gate columns n0.. then up columns N + n0.. of the expert
         const int up_shift = pr.epi == EPI_SWIGLU ? tb.N[tl.slot] - pr.bn / 2 : 0;
+        if (g.dep_role == 2) {
+          // rows of A written by problem 0 in this launch: wait for their row block
+          const int s0 = tl.slot - P.pr[0].g.E;  // the same expert in problem 0
+          const int blk = tb.mtp[s0] + tl.m0 / BMT;
+          const int need = 4 * ((tb.N[s0] + P.pr[0].tile_n - 1) / P.pr[0].tile_n);
+          if (blk >= g.dep_len) {
+            if (g.status != nullptr) atomicExch(g.status, kStatusBadArg);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_gpu(g.dep + blk) < need) {
+            if (abort_flag || global_timer_ns() - t0 > MOE_WAIT_NS) {
+              abort_flag = 1;
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // the TMA loads below see problem 0's stores
+          const int ntn = (tb.N[tl.slot] + pr.tile_n - 1) / pr.tile_n;
+          if (atomicAdd(g.dep + g.dep_len + blk, 1) == ntn - 1) {  // last reader
+            atomicExch(g.dep + blk, 0);
+            atomicExch(g.dep + g.dep_len + blk, 0);
+          }
+        }
         if (tl.p == 0)
           ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0],
                                          &P.tmB[0], nkb, am, ak, bn, bk, stage, phase, up_shift);
@@ -725,6 +763,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (rank == 0) mbar_arrive(&acc_empty[buf]);
         else mbar_arrive_remote(&acc_empty[buf], 0);
       }
+      if (g.dep_role == 1) {
+        // this warp's stores of the tile are complete and visible before its
+        // row block's count moves (the waiting problem loads them by TMA)
+        if (lane == 0) bulk_wait_group_all();
+        __syncwarp();
+        __threadfence();
+        if (lane == 0) {
+          fence_proxy_async_global();
+          const int blk = tb.mtp[slot] + tl.m0 / BMT;
+          if (blk < g.dep_len) atomicAdd(g.dep + blk, 1);
+        }
+      }
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
@@ -858,7 +908,17 @@ int launch_single(int c, const MultiParams& P, int grid, cudaStream_t st) {
 // (the backward pairs), any N tiles.  Returns kStatusUnsupported otherwise.
 template <typename T, int CG>
 int launch_pair(int c0, int c1, const MultiParams& P, int grid, cudaStream_t st) {
-  if ((c0 & 3) != 0 || (c1 & 3) != 3 || ((c0 | c1) & kCfgSwiglu)) return kStatusUnsupported;
+  if ((c0 | c1) & kCfgSwiglu) return kStatusUnsupported;
+  if ((c0 & 3) == 2 && (c1 & 3) == 2) {
+    // A K-major, B MN-major twice: the fused up + down projection
+    switch (((c0 >> 2) & 1) | (((c1 >> 2) & 1) << 1)) {
+      case 0: return launch<T, 2, 2, CG>(P, grid, st);
+      case 1: return launch<T, 6, 2, CG>(P, grid, st);
+      case 2: return launch<T, 2, 6, CG>(P, grid, st);
+      default: return launch<T, 6, 6, CG>(P, grid, st);
+    }
+  }
+  if ((c0 & 3) != 0 || (c1 & 3) != 3) return kStatusUnsupported;
   const int k = ((c0 >> 2) & 1) | (((c1 >> 2) & 1) << 1);
   switch (k) {
     case 0: return launch<T, 0, 3, CG>(P, grid, st);
@@ -922,7 +982,13 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   // CTA pairs (256-row tiles) only when every problem of the launch asks
   int cg = 2;
   for (int i = 0; i < n; ++i)
-    if (gs[i].E != 0 && (ops[i].pair != 2 || epis[i] == EPI_SWIGLU)) cg = 1;
+    if (gs[i].E != 0 && (ops[i].pair != 2 || epis[i] == EPI_SWIGLU || gs[i].dep_role != 0))
+      cg = 1;
+  // a dependent pair: problem 0 signals, problem 1 (same experts) waits
+  if (n == 2 && (gs[0].dep_role != 0 || gs[1].dep_role != 0) &&
+      (gs[0].dep_role != 1 || gs[1].dep_role != 2 || gs[0].E != gs[1].E || gs[0].E == 0 ||
+       gs[0].dep == nullptr || gs[0].dep != gs[1].dep))
+    return kStatusBadArg;
   for (int i = 0; i < n; ++i) {
     const GemmOperands& op = ops[i];
     const GroupedGemmDesc& g = gs[i];
@@ -981,6 +1047,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
                           : c0;
   int rc = dispatch_dtype(dtype, cg, used, c0, c1, P, grid, st);
   if (rc != kStatusUnsupported) return rc;
+  if (P.pr[0].g.dep_role != 0) return kStatusUnsupported;  // dependent pairs launch together
   // no compiled pair for these configurations: one launch per problem
   for (int i = 0; i < used; ++i) {
     MultiParams Q = P;

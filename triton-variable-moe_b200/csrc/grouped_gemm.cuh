@@ -62,6 +62,17 @@ struct GroupedGemmDesc {
   long long ld_aux2;
   long long aux2_rows;
   int* status;  // device status word: set non-zero when a wait gave up
+  // Row-block dependency between the two problems of one launch (dep_role 0:
+  // none).  The signalling problem (1) is problem 0: each of its epilogue warps
+  // adds 1 to dep[b] once its stores of a tile in row block b (expert e, rows
+  // [m, m + 128)) have completed.  The waiting problem (2) is problem 1, over
+  // the same experts and token rows: before loading a tile's A rows it waits
+  // until dep[b] counts every epilogue warp of every problem-0 tile of that row
+  // block.  dep[dep_len + b] counts the waiting tiles that passed; the last one
+  // returns both words to zero, so the buffer is zero again after the launch.
+  int* dep;
+  int dep_len;
+  int dep_role;
 };
 
 }  // namespace moe

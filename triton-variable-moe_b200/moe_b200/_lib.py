@@ -58,6 +58,9 @@ _SIGS = {
     "moe_grouped_gemm_up_swiglu": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _P, _P, _L, _I, _I,
                                    _P, _P],
     "moe_swiglu_grad": [_P, _P, _P, _L, _L, _P, _P, _I, _P, _L, _I, _P],
+    "moe_up_down_dep_words": [_L, _I],
+    "moe_grouped_gemm_up_down": [_P, _L, _L, _P, _P, _L, _L, _P, _P, _P, _I, _P, _P, _L, _P, _L, _P,
+                                 _L, _I, _I, _I, _P, _P],
     "moe_grouped_gemm_down": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _I, _I, _P, _P],
     "moe_grouped_gemm_up_dx": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _I, _I, _P, _P],
     "moe_grouped_gemm_up_dw": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _I, _P, _I, _I, _P, _P],
@@ -77,6 +80,7 @@ _RESTYPE = {
     "moe_status_string": c_char_p,
     "moe_route_workspace_bytes": c_int64,
     "moe_router_head_workspace_floats": c_int64,
+    "moe_up_down_dep_words": c_int64,
 }
 
 EXPORTED = tuple(_SIGS)

@@ -421,6 +421,42 @@ def swiglu_grad(grad_out, gate, up, tok_off, w_off, num_experts, out):
     return out
 
 
+_dep_buffers: dict = {}
+
+
+def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> torch.Tensor:
+    """Zeroed int32 row-block counters for gemm_up_down (every launch returns
+    them to zero); one per device, grown on demand."""
+    words = int(lib.moe_up_down_dep_words(rows, num_experts))
+    device = torch.device(device)
+    buf = _dep_buffers.get(device)
+    if buf is None or buf.numel() < words:
+        buf = torch.zeros(max(words, 1), dtype=torch.int32, device=device)
+        _dep_buffers[device] = buf
+    return buf
+
+
+def gemm_up_down(x, w1, w2, tok_off, w_off, tok_cnt, num_experts, inter, pre_act, out,
+                 tile_n_width=0, tile_n_hidden=0):
+    """inter = relu(x @ w1_e)^2 (pre_act = relu(x @ w1_e)), out = inter @ w2_e in
+    one launch; down tiles start as their row blocks of inter are complete."""
+    _gemm_check(x, w1, w2, inter, out)
+    tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
+    H, TW = w1.shape
+    dep = up_down_dep_buffer(x.device, x.shape[0], num_experts)
+    ev = _ev_begin()
+    rc = lib.moe_grouped_gemm_up_down(
+        ptr(x), x.shape[0], x.stride(0), ptr(w1), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
+        ptr(tok_cnt), int(num_experts), ptr(inter), ptr(pre_act), inter.stride(0), ptr(out),
+        out.stride(0), ptr(dep), dep.numel(), DTYPE_CODE[x.dtype], int(tile_n_width),
+        int(tile_n_hidden), ptr(status_buffer(x.device)), stream_handle(x.device),
+    )
+    _ev_end(ev, "grouped_gemm_up_down")
+    check(rc, "moe_grouped_gemm_up_down")
+    _count(1)
+    return out
+
+
 def gemm_down(inter, w2, tok_off, w_off, tok_cnt, num_experts, out, tile_n=0):
     _gemm_check(inter, w2, out)
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)

@@ -89,11 +89,11 @@ class _MoEMLPFunction(torch.autograd.Function):
         _ops.gather(x_flat, r.row_to_assignment, k, cap, out=xg, rows_device=p_dev)
         h = torch.empty(rows, plan.max_width, device=dev, dtype=dt)
         pre = torch.empty_like(h) if train else None
-        _ops.gemm_up(xg, w1, r.expert_token_offsets, plan.w_off, None, E, "relu_squared", h, pre,
-                     tile_n=plan.tile_n_width)
+        # up (relu^2) and down in one launch: down tiles start as soon as their
+        # rows of h are complete
         y = torch.empty(rows, H, device=dev, dtype=dt)
-        _ops.gemm_down(h, w2, r.expert_token_offsets, plan.w_off, None, E, y,
-                       tile_n=plan.tile_n_hidden)
+        _ops.gemm_up_down(xg, w1, w2, r.expert_token_offsets, plan.w_off, None, E, h, pre, y,
+                          tile_n_width=plan.tile_n_width, tile_n_hidden=plan.tile_n_hidden)
         out = _ops.combine(y, r.assignment_to_row, T, k, weights=weights)
 
         if train:
