@@ -23,7 +23,8 @@ experts are sharded over the ranks, with NCCL all-to-all dispatch and combine;
 that step runs eagerly because the exchange sizes are read on the host.
 
 Extra keys: `roofline` (the grouped-GEMM engine: algorithmic FLOPs
-12*H*sum_e n_e*w_e per step / summed device time of its 4 launches per step,
+12*H*sum_e n_e*w_e per step / summed device time of its launches per step (forward:
+up+down in one launch; backward: dIntermediate+dX, then dW2+dW1),
 against the measured bf16 peak), `cpu_baseline` (the numpy CPU oracle on the
 host cores), `e2e` (pinned host input -> device, fwd+bwd, output -> host,
 per step), `gpu_launches`, `clocks`.
@@ -501,13 +502,14 @@ def run_b200(args, cfg, name):
                 per_kind[kname] = per_kind.get(kname, 0.0) + a.elapsed_time(b) / reps
     gemm_ms = sum(v for k, v in per_kind.items() if k.startswith("grouped_gemm"))
     perm_ms = sum(v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
-    n_gemm_launches = 4
+    gemm_names = [kname for kname, _, _ in evs if kname.startswith("grouped_gemm")]
+    n_gemm_launches = max(len(gemm_names), 1)
     peak_tf, peak_hbm, peak_kind = measured_peaks()
     achieved = flops / (gemm_ms / 1e3) / 1e12
     traffic_step = ncu_traffic(name)
     roofline = {
-        "kernel": "grouped_gemm_kernel (tcgen05; 4 launches per step: up, down, "
-                  "down-dX + down-dW, up-dX + up-dW; 6 GEMMs)",
+        "kernel": f"grouped_gemm_kernel (tcgen05; {n_gemm_launches} launches per step: "
+                  f"{', '.join(gemm_names)}; 6 GEMMs)",
         "bound": "tensor",
         "achieved": achieved,
         "peak": peak_tf,
