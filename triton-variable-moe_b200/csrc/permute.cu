@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
 // out[t, :] = sum_j round(y[row(t,j), :] * w[t*k+j])  (fp32 sum, one rounding).
 // A warp combines R tokens at a time: lanes fetch the R * kMaxK row indices
 // and weights together, then all source-row vectors are loaded before any is
-// used.  Top-k beyond kMaxK runs in further batches of kMaxK.
-template <typename T, bool VEC, int kMaxK, int R>
+// used; NV 16-byte vectors per lane and source row cover 256*NV columns per
+// pass (one pass for the usual hidden sizes).  Top-k beyond kMaxK runs in
+// further batches of kMaxK.
+template <typename T, bool VEC, int kMaxK, int R, int NV>
 __global__ void __launch_bounds__(kThreadsPerBlock)
     combine_kernel(const T* __restrict__ y, long long ldy, int H,
                    const int32_t* __restrict__ asg_row, long long T_tokens, int k,
@@ -185,7 +187,6 @@ __global__ void __launch_bounds__(kThreadsPerBlock)
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const long long wid = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  constexpr int NV = VEC ? 2 : 1;  // 16-byte vectors per lane per source row and batch
   for (long long t0 = wid * R; t0 < T_tokens; t0 += warps * R) {
     if constexpr (VEC) {
       for (int c0 = 0; c0 < H; c0 += 32 * 8 * NV) {
@@ -420,23 +421,34 @@ int combine_t(const void* y, long long ldy, int H, const int32_t* asg_row, long 
   const T* yp = static_cast<const T*>(y);
   const T* wp = static_cast<const T*>(w);
   T* op = static_cast<T*>(out);
-  // tokens per warp batch: R * kMaxK source rows in flight (at most 8)
-#define MOE_COMBINE(KM, R)                                                                     \
+  // R tokens per warp batch and NV vectors per lane and source row: at most
+  // 4 * 256 columns per pass for top-k <= 2, 2 * 256 beyond (register budget).
+  // One token per warp measured faster than two at top-2 (more warps in flight).
+  const int nv = (H + 255) / 256;
+#define MOE_COMBINE_NV(KM, R, NV)                                                              \
   do {                                                                                         \
     const int grid = grid_for((T_tokens + (R) - 1) / (R), kThreadsPerBlock / 32);              \
     if constexpr (sizeof(T) == 2) {                                                            \
       if (vec)                                                                                 \
-        return launch_pdl(combine_kernel<T, true, KM, R>, grid, st, yp, ldy, H, asg_row,       \
+        return launch_pdl(combine_kernel<T, true, KM, R, NV>, grid, st, yp, ldy, H, asg_row,   \
                           T_tokens, k, wp, op, ldo);                                           \
     }                                                                                          \
-    return launch_pdl(combine_kernel<T, false, KM, R>, grid, st, yp, ldy, H, asg_row, T_tokens, \
-                      k, wp, op, ldo);                                                         \
+    return launch_pdl(combine_kernel<T, false, KM, R, 1>, grid, st, yp, ldy, H, asg_row,       \
+                      T_tokens, k, wp, op, ldo);                                               \
+  } while (0)
+#define MOE_COMBINE(KM, R)                \
+  do {                                    \
+    if (nv <= 1) MOE_COMBINE_NV(KM, R, 1); \
+    if (nv <= 2) MOE_COMBINE_NV(KM, R, 2); \
+    if (nv <= 3) MOE_COMBINE_NV(KM, R, 3); \
+    MOE_COMBINE_NV(KM, R, 4);             \
   } while (0)
   if (k <= 1) MOE_COMBINE(1, 2);
-  if (k <= 2) MOE_COMBINE(2, 2);
-  if (k <= 4) MOE_COMBINE(4, 1);
-  MOE_COMBINE(8, 1);
+  if (k <= 2) MOE_COMBINE(2, 1);
+  if (k <= 4) MOE_COMBINE_NV(4, 1, 2);
+  MOE_COMBINE_NV(8, 1, 2);
 #undef MOE_COMBINE
+#undef MOE_COMBINE_NV
 }
 
 
