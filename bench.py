@@ -266,19 +266,28 @@ def time_cpu_oracle(cfg, budget_s=15.0, tokens=None):
     return tokens / dt, tokens, reps
 
 
-def build_ep_layer(cfg, device, seed=0):
+def build_ep_layer(cfg, device, seed=0, calib_x=None):
     """The same layer (same seed, same full weights) with its experts sharded over
-    the ranks of the default process group."""
+    the ranks of the default process group.  With calib_x (this rank's tokens),
+    the experts are placed by the load the router gives them over all ranks'
+    tokens (ExpertParallelMoEMLP expert_loads); else round-robin."""
     import torch
 
     from moe_b200 import TritonMoEConfig
-    from moe_b200.ep import ExpertParallelMoEMLP
+    from moe_b200.ep import ExpertParallelMoEMLP, measure_expert_loads
 
     torch.manual_seed(seed)
     mcfg = TritonMoEConfig(n_embd=cfg["n_embd"], expert_sizes=cfg["expert_sizes"],
                            num_active_experts=cfg["top_k"], block_size=64)
     full = build_layer(cfg, "cpu", seed)
-    layer = ExpertParallelMoEMLP(mcfg)
+    loads = None
+    if calib_x is not None:
+        import copy
+
+        router = copy.deepcopy(full.router).to(device=device, dtype=calib_x.dtype)
+        loads = measure_expert_loads(router, calib_x, cfg["top_k"])
+        del router
+    layer = ExpertParallelMoEMLP(mcfg, expert_loads=loads)
     if cfg["zipf"]:
         layer.router = full.router
     layer.load_full_state_dict({k: v.float() for k, v in full.state_dict().items()})
@@ -382,10 +391,15 @@ def run_b200(args, cfg, name):
     T = cfg["batch"] * cfg["seq"]
     H = cfg["n_embd"]
     ep = ws > 1 and cfg.get("ep", False)  # expert parallel; else one replica per GPU
-    layer = build_ep_layer(cfg, dev, seed=0) if ep else build_layer(cfg, dev, seed=0)
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
     x_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
     g_host = torch.randn(cfg["batch"], cfg["seq"], H, generator=g).to(torch.bfloat16).pin_memory()
+    if ep:
+        calib = x_host.to(dev) if args.placement == "load" else None
+        layer = build_ep_layer(cfg, dev, seed=0, calib_x=calib)
+        del calib
+    else:
+        layer = build_layer(cfg, dev, seed=0)
     x = x_host.to(dev).requires_grad_(True)
     gout = g_host.to(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -648,7 +662,10 @@ def run_b200(args, cfg, name):
                 "global_batch": cfg["batch"] * ws,
                 "seq_len": cfg["seq"],
                 "parallelism": (f"expert parallel over {ws} GPUs ({layer.num_experts} experts "
-                                f"sharded, NCCL all-to-all dispatch/combine), {T} tokens per GPU")
+                                f"sharded, NCCL all-to-all dispatch/combine), {T} tokens per GPU, "
+                                + ("experts placed by the router's measured load over these "
+                                   "tokens" if args.placement == "load" else
+                                   "round-robin expert placement"))
                 if ep else (f"{ws} independent replicas, {T} tokens each, no collective (the "
                             "config's experts fit one GPU; expert parallelism is the c5 "
                             "config)") if ws > 1 else "single GPU",
@@ -686,6 +703,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", choices=["load", "round-robin"], default="load",
+                    help="expert placement of the expert-parallel config")
     ap.add_argument("--profile-step", action="store_true",
                     help="run the warm-up steps plus one eager step, print nothing (for ncu)")
     args = ap.parse_args()

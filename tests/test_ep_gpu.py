@@ -28,7 +28,7 @@ def _close(a, b, what):
     assert not bad.any(), f"{what}: {int(bad.sum())} mismatches, max err {(a - b).abs().max():.3e}"
 
 
-def _worker(rank, world, port, sizes, q):
+def _worker(rank, world, port, sizes, q, placement="round-robin"):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -47,7 +47,10 @@ def _worker(rank, world, port, sizes, q):
         with torch.no_grad():
             for p in (ref.router.weight, ref.w1, ref.w2):
                 p.normal_(0, 0.02)
-        ep = ExpertParallelMoEMLP(cfg)
+        loads = None
+        if placement == "load":  # a skewed placement: rank 0 gets the busiest experts' rows
+            loads = [float((e * 7) % 5 + 1) for e in range(ref.num_experts)]
+        ep = ExpertParallelMoEMLP(cfg, expert_loads=loads)
         ep.load_full_state_dict(ref.state_dict())
         ref = ref.to(dev, torch.bfloat16)
         ep = ep.to(dev, torch.bfloat16)
@@ -84,12 +87,14 @@ def _worker(rank, world, port, sizes, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("placement", ["round-robin", "load"])
 @pytest.mark.parametrize("sizes", [[(8, 512)], [(4, 512), (8, 256), (4, 128)]])
-def test_ep_matches_single_gpu_layer(sizes):
+def test_ep_matches_single_gpu_layer(sizes, placement):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, sizes, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, sizes, q, placement))
+             for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=600) for _ in procs)

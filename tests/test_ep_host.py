@@ -25,6 +25,39 @@ def test_shard_experts_balances_each_width_group():
     assert all(len(o) == 2 for o in owners)
 
 
+def test_shard_experts_by_load():
+    """Load-balanced placement: every expert once, every rank at least one,
+    deterministic, and the busiest rank within the longest-processing-time bound
+    (average + the largest single expert's work)."""
+    from moe_b200.ep import rank_major_order, shard_experts
+
+    sizes = [(32, 2048), (64, 1024), (32, 512)]
+    widths = [w for c, w in sizes for _ in range(c)]
+    g = torch.Generator().manual_seed(3)
+    loads = (torch.rand(128, generator=g) ** 4 * 1000).round()  # skewed, with ties at 0
+    for world in (1, 2, 4, 8):
+        owners = shard_experts(sizes, world, loads)
+        assert owners == shard_experts(sizes, world, loads.tolist())
+        assert sorted(e for o in owners for e in o) == list(range(128))
+        assert all(len(o) > 0 for o in owners) and all(o == sorted(o) for o in owners)
+        assert sorted(rank_major_order(owners)) == list(range(128))
+        work = [float(loads[e]) * widths[e] for e in range(128)]
+        per = [sum(work[e] for e in o) for o in owners]
+        assert max(per) <= sum(work) / world + max(work) + 1e-6
+        rr = shard_experts(sizes, world)
+        rr_per = [sum(work[e] for e in o) for o in rr]
+        assert max(per) <= max(rr_per) + 1e-6
+    # one hot expert: it gets a rank of its own
+    hot = [0.0] * 8
+    hot[5] = 100.0
+    owners = shard_experts([(8, 64)], 4, hot)
+    assert [5] in owners and all(len(o) > 0 for o in owners)
+    with pytest.raises(ValueError):
+        shard_experts([(8, 64)], 2, [1.0] * 7)
+    with pytest.raises(ValueError):
+        shard_experts([(8, 64)], 2, [-1.0] + [1.0] * 7)
+
+
 def test_split_sizes():
     from moe_b200.ep import split_sizes
 
@@ -81,6 +114,20 @@ def _worker(rank, world, port, q):
         for key in ("router.weight", "w1", "w2"):
             assert torch.equal(full[key], ref.state_dict()[key]), key
         assert ep.w1.shape[1] == sum(ep.expert_widths[e] for e in ep.local_experts)
+        # measured loads are summed over the ranks; a placement from them
+        # round-trips the state_dict too
+        from moe_b200.ep import measure_expert_loads
+
+        x = torch.randn(64, 32, generator=torch.Generator().manual_seed(rank))
+        loads = measure_expert_loads(ref.router, x, 2)
+        mine = torch.bincount(ref.router(x).topk(2, dim=-1).indices.reshape(-1), minlength=5)
+        assert loads.shape == (5,) and float(loads.sum()) == 2 * 64 * 2
+        assert bool((loads >= mine.double()).all())
+        epl = ExpertParallelMoEMLP(cfg, expert_loads=loads)
+        epl.load_full_state_dict(ref.state_dict())
+        full = epl.full_state_dict()
+        for key in ("router.weight", "w1", "w2"):
+            assert torch.equal(full[key], ref.state_dict()[key]), key
         q.put((rank, "ok"))
     except Exception as exc:  # reported to the parent
         q.put((rank, repr(exc)))

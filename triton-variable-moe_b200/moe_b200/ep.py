@@ -17,9 +17,15 @@ row counts of the exchange are read on the host once per direction (NCCL's
 all-to-all takes host split sizes), so an expert-parallel step synchronises
 the host once in the forward; the single-GPU layer does not.
 
-Expert placement (`shard_experts`): round-robin within each (count, width)
-group of the config, continuing the rank counter across groups, so every rank
-gets a near-equal share of each width class (parameters and FLOPs).
+Expert placement (`shard_experts`): by default round-robin within each
+(count, width) group of the config, continuing the rank counter across
+groups, so every rank gets a near-equal share of each width class
+(parameters, and FLOPs under uniform routing).  Under skewed routing the
+ranks that own the popular experts receive more rows, and every all-to-all
+waits for the busiest rank; given measured per-expert token counts
+(`expert_loads`, e.g. the all-reduced tokens_per_expert of a calibration
+step), experts are placed greedily instead: in decreasing order of work
+(tokens x width), each to the rank with the least work so far.
 Expert-local weights are stored concatenated in the rank's local expert
 order; `full_state_dict()` / `load_full_state_dict()` convert to and from the
 reference's unsharded `w1`/`w2` layout.
@@ -42,17 +48,33 @@ from .kernels import _ops
 from .moe import TritonMoEConfig, TritonMoEMLP, _AuxLosses, _Plan, _RouterHead
 
 
-def shard_experts(expert_sizes, world_size: int) -> list[list[int]]:
-    """Global expert ids owned by each rank (round-robin within size groups)."""
+def shard_experts(expert_sizes, world_size: int, loads=None) -> list[list[int]]:
+    """Global expert ids owned by each rank, ascending within a rank.
+
+    loads None: round-robin within size groups.  loads (per-expert token
+    counts, any non-negative numbers): longest-processing-time-first greedy
+    placement of the work loads[e] * width[e]; the first world_size experts
+    of that order go to distinct ranks, so every rank owns at least one expert
+    when there are at least as many experts as ranks.  Ties (equal work, equal
+    rank totals) resolve to the lower expert id and the lower rank, so every
+    rank computes the same placement."""
     owners: list[list[int]] = [[] for _ in range(world_size)]
-    eid = 0
-    r = 0
-    for count, _width in expert_sizes:
-        for _ in range(count):
-            owners[r % world_size].append(eid)
-            eid += 1
-            r += 1
-    return owners
+    widths = [w for count, w in expert_sizes for _ in range(count)]
+    if loads is None:
+        for eid in range(len(widths)):
+            owners[eid % world_size].append(eid)
+        return owners
+    loads = [float(v) for v in (loads.tolist() if hasattr(loads, "tolist") else loads)]
+    if len(loads) != len(widths) or any(not (v >= 0) for v in loads):
+        raise ValueError("expert_loads needs one non-negative value per expert")
+    work = [loads[e] * widths[e] for e in range(len(widths))]
+    total = [0.0] * world_size
+    for e in sorted(range(len(widths)), key=lambda e: (-work[e], e)):
+        # ranks still without an expert first, then the least total work
+        r = min(range(world_size), key=lambda j: (len(owners[j]) > 0, total[j], j))
+        owners[r].append(e)
+        total[r] += work[e]
+    return [sorted(o) for o in owners]
 
 
 def rank_major_order(owners: list[list[int]]) -> list[int]:
@@ -195,6 +217,20 @@ class _EPMoEFunction(torch.autograd.Function):
         return gx, gw1, gw2, None, None, None
 
 
+@torch.no_grad()
+def measure_expert_loads(router: nn.Module, x: torch.Tensor, top_k: int, group=None) -> torch.Tensor:
+    """Tokens routed to each expert by `router` over this rank's tokens x
+    [..., n_embd], summed over the ranks of `group` (collective): the
+    expert_loads of a load-balanced placement.  top-k of the logits is the
+    top-k of the sigmoid probabilities the layer routes on."""
+    logits = router(x.reshape(-1, x.shape[-1]))
+    sel = logits.float().topk(top_k, dim=-1).indices.reshape(-1)
+    counts = torch.bincount(sel, minlength=logits.shape[-1]).to(torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(counts, group=group)
+    return counts.cpu()
+
+
 class ExpertParallelMoEMLP(nn.Module):
     """TritonMoEMLP with its experts sharded over the ranks of `group`.
 
@@ -202,10 +238,11 @@ class ExpertParallelMoEMLP(nn.Module):
     the experts `shard_experts` gives it.  forward(x) takes this rank's tokens
     [batch, seq, n_embd] and returns (output, aux_loss, f_i) like
     TritonMoEMLP, with the auxiliary losses and f_i computed over this rank's
-    tokens.
+    tokens.  expert_loads (the same on every rank; see `measure_expert_loads`)
+    switches the expert placement from round-robin to load-balanced.
     """
 
-    def __init__(self, config: TritonMoEConfig, group=None):
+    def __init__(self, config: TritonMoEConfig, group=None, expert_loads=None):
         super().__init__()
         if not dist.is_initialized():
             raise RuntimeError("ExpertParallelMoEMLP needs an initialised torch.distributed group")
@@ -219,7 +256,7 @@ class ExpertParallelMoEMLP(nn.Module):
         self.norm_topk_prob = full.norm_topk_prob
         self.block_size = full.block_size
         self.expert_widths = full.expert_widths
-        self.owners = shard_experts(config.expert_sizes, self.world)
+        self.owners = shard_experts(config.expert_sizes, self.world, expert_loads)
         if any(len(o) == 0 for o in self.owners):
             raise ValueError("every rank needs at least one expert")
         self.local_experts = self.owners[self.rank]
