@@ -101,3 +101,18 @@ def test_ep_matches_single_gpu_layer(sizes, placement):
     for p in procs:
         p.join(timeout=120)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+@pytest.mark.parametrize("placement", ["round-robin", "load"])
+def test_ep_world1_matches_single_gpu_layer(placement):
+    """The expert-parallel layer on one rank (NCCL world of 1: the exchanges are
+    local copies) against the single-GPU layer: runs on a one-GPU machine too."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    p = ctx.Process(target=_worker, args=(0, 1, port, [(4, 512), (8, 256), (4, 128)], q,
+                                          placement))
+    p.start()
+    results = dict([q.get(timeout=600)])
+    p.join(timeout=120)
+    assert results == {0: "ok"}, results

@@ -161,11 +161,10 @@ class _EPMoEFunction(torch.autograd.Function):
         _ops.gather(src, lr.row_to_assignment, 1, lr.p_capacity, out=xg, rows_device=p_dev)
         h = torch.empty(cap, lp.max_width, device=dev, dtype=dt)
         pre = torch.empty_like(h) if train else None
-        _ops.gemm_up(xg, w1, lr.expert_token_offsets, lp.w_off, None, e_loc, "relu_squared", h,
-                     pre, tile_n=lp.tile_n_width)
+        # up (relu^2) and down in one launch, as in the single-GPU layer
         y = torch.empty(cap, H, device=dev, dtype=dt)
-        _ops.gemm_down(h, w2, lr.expert_token_offsets, lp.w_off, None, e_loc, y,
-                       tile_n=lp.tile_n_hidden)
+        _ops.gemm_up_down(xg, w1, w2, lr.expert_token_offsets, lp.w_off, None, e_loc, h, pre, y,
+                          tile_n_width=lp.tile_n_width, tile_n_hidden=lp.tile_n_hidden)
         y_recv = _ops.combine(y, lr.assignment_to_row, R, 1, weights=None)
         # 4. results back to the source ranks, weighted combine of the k copies
         ys = exchange_rows(y_recv, recv, send, plan.group)
