@@ -13,7 +13,8 @@
 //                  (block 0 also writes the per-expert outputs and padding-row
 //                  markers), then each warp ranks its unit stably (match_any)
 //                  and writes the sorted order and both row maps
-// Problems of at most 8192 assignments run all phases in one CTA.
+// Problems of at most 6144 assignments run all phases in one CTA (its time grows
+// with the assignments; past ~7000 the two multi-block launches are faster).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 // owns the contiguous chunk [w*U, (w+1)*U) of assignments; its per-expert
 // histogram row in shared memory becomes its running rank base.
 constexpr int kSmallWarps = 32;
-constexpr long long kSmallMaxA = 8192;
+constexpr long long kSmallMaxA = 6144;
 
 template <typename S>
 __global__ void __launch_bounds__(kSmallWarps * 32, 1)

@@ -151,7 +151,7 @@ def route(
     )
     _ev_end(ev, "route")
     check(rc, "moe_route")
-    _count(1 if A <= 8192 else 2)  # one fused CTA for small problems
+    _count(1 if A <= 6144 else 2)  # one fused CTA for small problems
     return Routing(bin_ids, indices, tpe, bins, pbins, tok_off, ptpe, row_asg, asg_row, cap)
 
 
