@@ -57,7 +57,9 @@ def _worker(rank, world, port, sizes, q, placement="round-robin"):
         g = torch.Generator(device="cpu").manual_seed(1)
         xg = torch.randn(world, T, H, generator=g).to(dev, torch.bfloat16)
         gg = torch.randn(world, T, H, generator=g).to(dev, torch.bfloat16)
-        for _ in range(2):  # twice: the second step reuses every cached plan
+        for it in range(3):  # the second step reuses every cached plan
+            if it == 2:  # then re-place the experts (weights move with them)
+                ep.rebalance([float(ref.num_experts - e) for e in range(ref.num_experts)])
             ep.zero_grad(set_to_none=True)
             ref.zero_grad(set_to_none=True)
             x = xg[rank : rank + 1].clone().requires_grad_()

@@ -128,6 +128,19 @@ def _worker(rank, world, port, q):
         full = epl.full_state_dict()
         for key in ("router.weight", "w1", "w2"):
             assert torch.equal(full[key], ref.state_dict()[key]), key
+        # re-placement by other loads moves the weights with their experts
+        from moe_b200.ep import shard_experts
+
+        new_loads = [1.0, 50.0, 2.0, 40.0, 3.0]
+        epl.rebalance(new_loads)
+        assert epl.owners == shard_experts(cfg.expert_sizes, world, new_loads)
+        assert epl.local_experts == epl.owners[rank]
+        assert epl.w1.shape[1] == sum(epl.expert_widths[e] for e in epl.local_experts)
+        assert int(epl.local_weight_offsets[-1]) == epl.w1.shape[1]
+        full = epl.full_state_dict()
+        for key in ("router.weight", "w1", "w2"):
+            assert torch.equal(full[key], ref.state_dict()[key]), key
+        assert sorted(epl.global_of_rank_major.tolist()) == list(range(5))
         q.put((rank, "ok"))
     except Exception as exc:  # reported to the parent
         q.put((rank, repr(exc)))

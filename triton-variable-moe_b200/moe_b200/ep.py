@@ -255,33 +255,50 @@ class ExpertParallelMoEMLP(nn.Module):
         self.norm_topk_prob = full.norm_topk_prob
         self.block_size = full.block_size
         self.expert_widths = full.expert_widths
-        self.owners = shard_experts(config.expert_sizes, self.world, expert_loads)
-        if any(len(o) == 0 for o in self.owners):
-            raise ValueError("every rank needs at least one expert")
-        self.local_experts = self.owners[self.rank]
         self.router = full.router
-        w1, w2 = self._slice(full.w1.data, full.w2.data)
+        self.register_buffer("expert_widths_normalized", full.expert_widths_normalized.clone(),
+                             persistent=False)
+        self._lb_coef_values = full._lb_coef_values
+        self._place(shard_experts(config.expert_sizes, self.world, expert_loads),
+                    full.w1.data, full.w2.data)
+
+    def _place(self, owners, w1_full: torch.Tensor, w2_full: torch.Tensor) -> None:
+        """Adopt an expert placement: this rank's expert weights sliced from the
+        unsharded w1 / w2, and the id maps and offsets the forward uses."""
+        if any(len(o) == 0 for o in owners):
+            raise ValueError("every rank needs at least one expert")
+        self.owners = owners
+        self.local_experts = owners[self.rank]
+        w1, w2 = self._slice(w1_full, w2_full)
         self.w1 = nn.Parameter(w1)
         self.w2 = nn.Parameter(w2)
-        order = rank_major_order(self.owners)
+        dev = w1.device
+        order = rank_major_order(owners)
         inv = [0] * self.num_experts
         for pos, e in enumerate(order):
             inv[e] = pos
-        self.register_buffer("rank_major_of_global", torch.tensor(inv, dtype=torch.long),
-                             persistent=False)
-        self.register_buffer("global_of_rank_major", torch.tensor(order, dtype=torch.long),
-                             persistent=False)
+        self.register_buffer("rank_major_of_global",
+                             torch.tensor(inv, dtype=torch.long, device=dev), persistent=False)
+        self.register_buffer("global_of_rank_major",
+                             torch.tensor(order, dtype=torch.long, device=dev), persistent=False)
         lw = [self.expert_widths[e] for e in self.local_experts]
         loff = [0]
         for w in lw:
             loff.append(loff[-1] + w)
-        self.register_buffer("local_weight_offsets", torch.tensor(loff, dtype=torch.int32),
-                             persistent=False)
-        self.register_buffer("expert_widths_normalized", full.expert_widths_normalized.clone(),
-                             persistent=False)
-        self._lb_coef_values = full._lb_coef_values
+        self.register_buffer("local_weight_offsets",
+                             torch.tensor(loff, dtype=torch.int32, device=dev), persistent=False)
         self._local_widths = lw
         self._plan_cache: _EPPlan | None = None
+
+    def rebalance(self, expert_loads) -> None:
+        """Re-place the experts by new loads (collective: every rank calls it with
+        the same loads, e.g. from `measure_expert_loads`).  The weights move with
+        their experts; w1 and w2 become new Parameters (rebuild the optimizer over
+        them), and gradients are dropped."""
+        owners = shard_experts(self.config.expert_sizes, self.world, expert_loads)
+        full = self.full_state_dict()
+        dtype = self.w1.dtype
+        self._place(owners, full["w1"].to(dtype), full["w2"].to(dtype))
 
     def _lb_coef(self, device) -> torch.Tensor:
         return TritonMoEMLP._lb_coef(self, device)
