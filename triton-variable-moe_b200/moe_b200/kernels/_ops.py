@@ -426,7 +426,8 @@ _dep_buffers: dict = {}
 
 def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> torch.Tensor:
     """Zeroed int32 row-block counters for gemm_up_down (every launch returns
-    them to zero); one per device, grown on demand."""
+    them to zero); one per device, grown on demand, so gemm_up_down launches on
+    one device must not overlap (different streams without ordering)."""
     words = int(lib.moe_up_down_dep_words(rows, num_experts))
     device = torch.device(device)
     buf = _dep_buffers.get(device)
