@@ -422,6 +422,9 @@ def swiglu_grad(grad_out, gate, up, tok_off, w_off, num_experts, out):
 
 
 _dep_buffers: dict = {}
+# replaced (smaller) counter buffers stay allocated: a CUDA graph captured with
+# one keeps its address
+_dep_buffers_retired: list = []
 
 
 def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> torch.Tensor:
@@ -432,6 +435,13 @@ def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> tor
     device = torch.device(device)
     buf = _dep_buffers.get(device)
     if buf is None or buf.numel() < words:
+        if torch.cuda.is_current_stream_capturing():
+            # a zero fill recorded into a graph runs only at replay
+            raise RuntimeError(
+                "gemm_up_down: run the layer once eagerly at this size before capturing "
+                "it in a CUDA graph (its counter buffer is allocated on first use)")
+        if buf is not None:
+            _dep_buffers_retired.append(buf)
         buf = torch.zeros(max(words, 1), dtype=torch.int32, device=device)
         _dep_buffers[device] = buf
     return buf
