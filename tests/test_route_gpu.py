@@ -32,6 +32,11 @@ ROUTE_CASES = [
     (4096, 8, 128, "nearest", False),
     (777, 7, 32, "nearest", True),
     (3000, 1, 64, "up", False),
+    # the multi-block path (past the single-CTA bound) in every rounding mode
+    (6145, 8, 64, "up", False),
+    (16384, 16, 64, "down", True),
+    (10000, 7, 32, "nearest", True),
+    (65536, 64, 128, "down", False),
 ]
 
 
