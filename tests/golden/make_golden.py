@@ -165,14 +165,20 @@ def gen_swiglu(K, torch):
 
 
 def gen_layer(moe_mod, torch):
-    """The small CPU config (n_embd 64, 4 experts x 128, top-2, 2 x 16 tokens) and a
-    variable-width variant: full layer fwd + bwd."""
+    """The small CPU config (n_embd 64, 4 experts x 128, top-2, 2 x 16 tokens), a
+    variable-width variant, and variants without top-k renormalisation, with
+    top-1 and with block size 128: full layer fwd + bwd."""
     from triton_moe import TritonMoEConfig, TritonMoEMLP
 
     cases = {}
     specs = [
         ("c1", dict(n_embd=64, expert_sizes=[(4, 128)], num_active_experts=2), 2, 16, 0),
         ("c1v", dict(n_embd=64, expert_sizes=[(2, 128), (2, 64)], num_active_experts=2), 2, 24, 1),
+        ("c1n", dict(n_embd=64, expert_sizes=[(4, 128)], num_active_experts=2,
+                     norm_topk_prob=False), 2, 16, 2),
+        ("c1k1", dict(n_embd=64, expert_sizes=[(2, 128), (2, 64)], num_active_experts=1), 2, 16, 3),
+        ("c1b", dict(n_embd=64, expert_sizes=[(4, 128)], num_active_experts=2, block_size=128),
+         2, 16, 4),
     ]
     for name, cfg, B, S, seed in specs:
         torch.manual_seed(seed)
@@ -190,6 +196,7 @@ def gen_layer(moe_mod, torch):
             expert_sizes=np.array(cfg["expert_sizes"]),
             top_k=np.int64(cfg["num_active_experts"]),
             block_size=np.int64(m.block_size),
+            norm_topk_prob=np.int64(bool(m.norm_topk_prob)),
             router_w=np32(m.router.weight), w1=np32(m.w1), w2=np32(m.w2), x=np32(x),
             selected=np32(inter["selected_experts_flat"]), weights=np32(inter["top_k_weights_flat"]),
             out=np32(out), dx=np32(x.grad), dw1=np32(m.w1.grad), dw2=np32(m.w2.grad),

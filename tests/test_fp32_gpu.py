@@ -105,8 +105,10 @@ def test_fp32_layer_matches_reference_golden(case, device):
     d = LAYER[case]
     H = int(d["n_embd"])
     sizes = [tuple(int(v) for v in s) for s in d["expert_sizes"]]
+    norm = bool(int(d["norm_topk_prob"])) if "norm_topk_prob" in d else True
     m = TritonMoEMLP(TritonMoEConfig(n_embd=H, expert_sizes=sizes,
                                      num_active_experts=int(d["top_k"]),
+                                     norm_topk_prob=norm,
                                      block_size=int(d["block_size"]))).to(device)
     with torch.no_grad():
         m.router.weight.copy_(torch.from_numpy(d["router_w"]))
