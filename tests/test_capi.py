@@ -84,3 +84,37 @@ def test_binding_argument_types_match_prototypes():
             assert _lib._RESTYPE.get(name) is ctypes.c_char_p, name
         else:
             assert ret == "int" and name not in _lib._RESTYPE, (name, ret)
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/moe_b200.h compiles as C99 (no C++ or torch types), and a C program
+    taking the address of every declared entry point links against the library."""
+    import shutil
+    import subprocess
+
+    from moe_b200 import _lib
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        import pytest
+
+        pytest.skip("no C compiler")
+    names = declared()
+    src = tmp_path / "use_header.c"
+    src.write_text(
+        '#include "moe_b200.h"\n#include <stdio.h>\n'
+        "typedef void (*fn_t)(void);\n"
+        "int main(void) {\n  const fn_t fns[] = {\n"
+        + "".join(f"    (fn_t)&{n},\n" for n in names)
+        + "  };\n  printf(\"%d %s\\n\", (int)(sizeof(fns) / sizeof(fns[0])), moe_version());\n"
+        "  return 0;\n}\n")
+    exe = tmp_path / "use_header"
+    lib = Path(_lib.LIB_PATH)
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-pedantic", "-I", str(ROOT / "include"),
+                        str(src), "-o", str(exe), "-L", str(lib.parent), "-l:" + lib.name,
+                        "-Wl,-rpath," + str(lib.parent)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr[-2000:]
+    count, version = run.stdout.split(maxsplit=1)
+    assert int(count) == len(names) and version.startswith("moe_b200")
