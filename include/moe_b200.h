@@ -60,6 +60,17 @@ extern "C" {
 MOE_API const char* moe_version(void);
 MOE_API const char* moe_status_string(int status);
 
+/* Time limit, in nanoseconds, of every device-side wait of the grouped-GEMM
+ * kernels launched after this call (an mbarrier wait, or a fused up+down
+ * launch's wait for its row block of the intermediate); 0 restores the
+ * default of 2 s.  A wait that runs out sets MOE_ERR_TIMEOUT in the launch's
+ * `status` word, the kernel lets its own copies and MMAs in flight finish,
+ * releases its tensor memory and returns; its outputs are then undefined.
+ * No counterpart in the reference (its Triton kernels have no device waits);
+ * it exists so that a test can make a wait run out quickly.  Process-wide;
+ * returns the previous limit. */
+MOE_API uint64_t moe_set_wait_timeout_ns(uint64_t ns);
+
 /* Bytes of device workspace moe_route needs for `num_assignments` top-k
  * assignments over `num_experts` experts. */
 MOE_API int64_t moe_route_workspace_bytes(int64_t num_assignments, int num_experts);

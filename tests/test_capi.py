@@ -53,12 +53,14 @@ def prototypes():
 
 
 def _kind(param: str) -> str:
-    """ctypes kind of a C parameter declaration: pointer, int64 or int."""
+    """ctypes kind of a C parameter declaration: pointer, int64, uint64 or int."""
     if "*" in param:
         return "P"
     words = param.replace("const", " ").split()
     if words[0] in ("int64_t", "long"):
         return "L"
+    if words[0] == "uint64_t":
+        return "U"
     if words[0] in ("int", "unsigned"):
         return "I"
     raise AssertionError(f"unmapped parameter type: {param!r}")
@@ -71,7 +73,7 @@ def test_binding_argument_types_match_prototypes():
 
     from moe_b200 import _lib
 
-    kinds = {ctypes.c_void_p: "P", ctypes.c_int64: "L", ctypes.c_int: "I"}
+    kinds = {ctypes.c_void_p: "P", ctypes.c_int64: "L", ctypes.c_int: "I", ctypes.c_uint64: "U"}
     protos = prototypes()
     assert sorted(protos) == declared()
     for name, (ret, params) in protos.items():
@@ -80,6 +82,8 @@ def test_binding_argument_types_match_prototypes():
         assert got == want, (name, got, want)
         if ret.startswith("int64_t"):
             assert _lib._RESTYPE.get(name) is ctypes.c_int64, name
+        elif ret.startswith("uint64_t"):
+            assert _lib._RESTYPE.get(name) is ctypes.c_uint64, name
         elif "char" in ret:
             assert _lib._RESTYPE.get(name) is ctypes.c_char_p, name
         else:

@@ -133,3 +133,26 @@ def test_bf16_rounding_is_round_to_nearest_even():
     ])
     exp = torch.from_numpy(v).bfloat16().float().numpy()
     np.testing.assert_array_equal(orc.round_bf16(v), exp)
+
+
+@pytest.mark.parametrize("case", sorted(load("layer")))
+def test_aux_loss_checker_matches_reference(case):
+    """oracle.aux_reference (the torch checker of the fused aux-loss kernels)
+    reproduces the reference layer's z-loss, load-balance loss, compute loss
+    and f_i from the golden router weights and tokens."""
+    import torch
+
+    from oracle import aux_reference
+
+    d = load("layer")[case]
+    sizes = [tuple(int(v) for v in s) for s in d["expert_sizes"]]
+    E = sum(c for c, _ in sizes)
+    x = torch.from_numpy(d["x"]).reshape(-1, int(d["n_embd"]))
+    logits = x @ torch.from_numpy(d["router_w"]).T
+    probs = torch.sigmoid(logits)
+    tpe = torch.bincount(torch.from_numpy(d["selected"]).reshape(-1).long(), minlength=E)
+    aux, f_i = aux_reference.aux_losses(sizes, logits, probs, tpe, torch.float32)
+    np.testing.assert_allclose(f_i.numpy(), d["f_i"], rtol=1e-6)
+    np.testing.assert_allclose(aux["router_z_loss"].item(), d["z_loss"], rtol=1e-5)
+    np.testing.assert_allclose(aux["load_balance_loss"].item(), d["lb_loss"], rtol=1e-5)
+    np.testing.assert_allclose(aux["compute_loss"].item(), d["compute_loss"], rtol=1e-5)

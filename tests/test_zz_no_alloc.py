@@ -76,8 +76,9 @@ def _check_against_moe_route(sel: torch.Tensor, E: int, bs: int):
 
 def test_no_alloc_route_matches_route_twice(device):
     g = torch.Generator(device="cpu").manual_seed(5)
-    # first call: the largest scratch the entry point supports (256 units x 256 experts)
-    sel1 = torch.randint(0, 256, (300_000,), generator=g).to(device)
+    # first call: the largest scratch the entry point supports (256 units x 256
+    # experts): 256 * 1184 assignments make units of 1184, exactly 256 of them
+    sel1 = torch.randint(0, 256, (256 * 1184,), generator=g).to(device)
     _check_against_moe_route(sel1, 256, 64)
     # second call, different problem (int32 ids, skewed, fewer experts)
     p = 1.0 / torch.arange(1, 17, dtype=torch.float64) ** 1.1

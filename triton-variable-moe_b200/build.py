@@ -53,25 +53,32 @@ def _compile(src: Path, obj: Path, extra: list[str]) -> None:
     subprocess.run(cmd, check=True)
 
 
-def build(force: bool = False, jobs: int = 4, verbose_ptxas: bool = False) -> Path:
-    OBJ_DIR.mkdir(exist_ok=True)
+def build(force: bool = False, jobs: int = 4, verbose_ptxas: bool = False,
+          trace: bool = False) -> Path:
+    """Compile the library.  trace=True builds the GEMM timeline variant
+    (-DMOE_TRACE, exports moe_trace_read) as libmoe_b200_trace.so instead."""
+    obj_dir = OBJ_DIR.with_name("_build_trace") if trace else OBJ_DIR
+    out = OUT.with_name("libmoe_b200_trace.so") if trace else OUT
+    obj_dir.mkdir(exist_ok=True)
     hdr = _headers_mtime()
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    if trace:
+        extra.append("-DMOE_TRACE")
     todo = []
     objs = []
     for s in SOURCES:
         src = CSRC / s
-        obj = OBJ_DIR / (s + ".o")
+        obj = obj_dir / (s + ".o")
         objs.append(obj)
         if force or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr):
             todo.append((src, obj))
     with cf.ThreadPoolExecutor(max_workers=max(1, jobs)) as ex:
         list(ex.map(lambda so: _compile(so[0], so[1], extra), todo))
-    if todo or force or not OUT.exists():
+    if todo or force or not out.exists():
         # exported symbols: only the extern "C" ABI (default visibility below)
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-Xcompiler", "-fPIC"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(out), *map(str, objs), "-Xcompiler", "-fPIC"]
         subprocess.run(cmd, check=True)
-    return OUT
+    return out
 
 
 if __name__ == "__main__":
@@ -79,6 +86,7 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-j", type=int, default=4)
     ap.add_argument("--ptxas-v", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="GEMM timeline build (-DMOE_TRACE)")
     a = ap.parse_args()
-    print(build(a.force, a.j, a.ptxas_v))
+    print(build(a.force, a.j, a.ptxas_v, a.trace))
     sys.exit(0)

@@ -89,6 +89,10 @@ bool common_ok(long long rows, long long hidden, long long total_width, const in
 
 extern "C" {
 
+uint64_t moe_set_wait_timeout_ns(uint64_t ns) {
+  return static_cast<uint64_t>(moe::set_wait_ns(static_cast<unsigned long long>(ns)));
+}
+
 const char* moe_version(void) { return "moe_b200 0.1 (sm_100a tcgen05)"; }
 
 const char* moe_status_string(int s) {

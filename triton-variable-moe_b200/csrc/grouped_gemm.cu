@@ -14,7 +14,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -22,6 +24,7 @@
 #include "grouped_gemm.cuh"
 #include "moe_internal.h"
 #include "sm100_ptx.cuh"
+#include "trace.cuh"
 
 namespace moe {
 
@@ -55,6 +58,7 @@ struct MultiParams {
   int stages;       // stages in the ring (depends on the largest N tile)
   int stage_bytes;  // A tile + largest B tile
   int smem_bytes;   // dynamic shared memory of the launch
+  unsigned long long wait_ns;  // limit of every device-side wait (ns)
 };
 
 // Per (problem, expert) slot: tile prefix, extents and the two offsets every
@@ -203,15 +207,17 @@ constexpr int cfg_of(int a_mn, int b_mn, int bn, bool swiglu = false) {
 template <int CFG, typename T, int CG>
 __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint64_t* full,
                                              uint64_t* empty, volatile int* abort_flag,
-                                             const void* tA, const void* tB, int nkb, int am,
-                                             int ak, int bn, int bk, int& stage,
-                                             uint32_t& phase, int up_shift) {
+                                             uint64_t wait_ns, const void* tA,
+                                             const void* tB, int nkb, int am, int ak, int bn,
+                                             int bk, int& stage, uint32_t& phase, int up_shift,
+                                             int& issued) {
   constexpr bool A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = ((CFG & 4) ? 256 : 128) / CG;  // B rows this CTA loads
   constexpr int BKE = Elem<T>::BKE;
   constexpr uint32_t bytes = kABytes + NT * 128;
   for (int kb = 0; kb < nkb; ++kb) {
-    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
+    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, wait_ns)) return false;
+    MOE_TRACE_KB(issued, 0);
     mbar_arrive_expect_tx(&full[stage], bytes);
     uint8_t* a_dst = ring + stage * SB;
     uint8_t* b_dst = a_dst + kABytes;
@@ -233,12 +239,31 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
     } else {
       tma_load_2d(b_dst, tB, &full[stage], bk + kc, bn);
     }
+    ++issued;
     if (++stage == S) {
       stage = 0;
       phase ^= 1;
     }
   }
   return true;
+}
+
+// After an abort: wait (bounded, ignoring the abort flag) until the stages
+// this producer loaded last have landed, so that no TMA write into shared
+// memory is in flight when the CTA exits.  (stage, phase) is the producer's
+// next write; `issued` counts the k-blocks it loaded.
+__device__ __forceinline__ void drain_loads(uint64_t* full, int S, int stage, uint32_t phase,
+                                            int issued, uint64_t wait_ns) {
+  int no_abort = 0;
+  for (int j = 0; j < S && j < issued; ++j) {
+    if (stage == 0) {
+      stage = S - 1;
+      phase ^= 1;
+    } else {
+      --stage;
+    }
+    mbar_wait(&full[stage], phase, &no_abort, wait_ns);
+  }
 }
 
 // MMA side of one tile: issue its k-blocks into the TMEM accumulator.
@@ -249,8 +274,9 @@ __device__ __forceinline__ bool produce_tile(uint8_t* ring, int SB, int S, uint6
 template <int CFG, typename T, int CG>
 __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t* full,
                                          uint64_t* peer_full, uint64_t* empty,
-                                         volatile int* abort_flag, uint32_t d_tmem, int K,
-                                         int nkb, int& stage, uint32_t& phase) {
+                                         volatile int* abort_flag, uint64_t wait_ns,
+                                         uint32_t d_tmem, int K,
+                                         int nkb, int& stage, uint32_t& phase, int& seen) {
   constexpr int A_MN = CFG & 1, B_MN = (CFG >> 1) & 1;
   constexpr int NT = (CFG & 4) ? 256 : 128;
   constexpr int BKE = Elem<T>::BKE, UKE = Elem<T>::UKE;
@@ -264,9 +290,11 @@ __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t*
   constexpr uint32_t a_sbo = (A_MN && kW) ? 512u : 1024u, a_lay = (A_MN && kW) ? 1u : 2u;
   constexpr uint32_t b_sbo = (B_MN && kW) ? 512u : 1024u, b_lay = (B_MN && kW) ? 1u : 2u;
   for (int kb = 0; kb < nkb; ++kb) {
-    if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
+    if (!mbar_wait(&full[stage], phase, abort_flag, wait_ns)) return false;
     if constexpr (CG == 2)
-      if (!mbar_wait_cluster(&peer_full[stage], phase, abort_flag)) return false;
+      if (!mbar_wait_cluster(&peer_full[stage], phase, abort_flag, wait_ns)) return false;
+    MOE_TRACE_KB(seen, 1);
+    ++seen;
     tc_fence_after();
     const uint32_t a_addr = smem_u32(ring + stage * SB);
     const uint32_t b_addr = a_addr + kABytes;
@@ -319,6 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint64_t wait_ns = P.wait_ns;
+  // waits that must complete even after an abort (this CTA's own copies and
+  // MMAs in flight) see this flag, which stays 0, and only their time limit
+  int no_abort = 0;
+  if (threadIdx.x == 0) MOE_TRACE_AT(0);
   // (problem, expert) slots: problem 0's experts, then problem 1's
   const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
   Table tb;
@@ -428,14 +461,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // from here on the kernel reads and writes global memory that the preceding
   // kernel may produce or consume: wait for it (programmatic dependent launch)
   griddep_wait();
+  if (threadIdx.x == 0) MOE_TRACE_AT(1);
   // a pair's barriers are initialised before either CTA signals the other's
   if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
+  if (threadIdx.x == 0) MOE_TRACE_AT(59);
   // The next kernel may start its own prologue now; it waits for this grid's
   // completion before touching memory.
   griddep_launch_dependents();
+  if (threadIdx.x == 0) MOE_TRACE_AT(60);
   const uint32_t tmem_base = *tmem_slot;
   const int total = tb.prefix[nge];
+  if (threadIdx.x == 0 && total >= 0) MOE_TRACE_AT(61);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -443,7 +480,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += nunits) {
+      int ti = 0, issued = 0;
+      for (int t = unit; t < total && ok; t += nunits, ++ti) {
+        MOE_TRACE_TILE(ti, 0);
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const Problem& pr = P.pr[tl.p];
         const GroupedGemmDesc& g = pr.g;
@@ -469,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint64_t t0 = global_timer_ns();
           while (ld_acquire_gpu(g.dep + blk) < need) {
-            if (abort_flag || global_timer_ns() - t0 > MOE_WAIT_NS) {
+            if (abort_flag || global_timer_ns() - t0 > wait_ns) {
               abort_flag = 1;
               ok = false;
               break;
@@ -477,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           fence_proxy_async_global();  // the TMA loads below see problem 0's stores
+          MOE_TRACE_TILE(ti, 1);
           const int ntn = (tb.N[tl.slot] + pr.tile_n - 1) / pr.tile_n;
           if (atomicAdd(g.dep + g.dep_len + blk, 1) == ntn - 1) {  // last reader
             atomicExch(g.dep + blk, 0);
@@ -484,12 +524,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (tl.p == 0)
-          ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[0],
-                                         &P.tmB[0], nkb, am, ak, bn, bk, stage, phase, up_shift);
+          ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, wait_ns, &P.tmA[0],
+                                         &P.tmB[0], nkb, am, ak, bn, bk, stage, phase, up_shift,
+                                         issued);
         else
-          ok = produce_tile<CFG1, T, CG>(ring, SB, S, full, empty, &abort_flag, &P.tmA[1],
-                                         &P.tmB[1], nkb, am, ak, bn, bk, stage, phase, up_shift);
+          ok = produce_tile<CFG1, T, CG>(ring, SB, S, full, empty, &abort_flag, wait_ns, &P.tmA[1],
+                                         &P.tmB[1], nkb, am, ak, bn, bk, stage, phase, up_shift,
+                                         issued);
+        MOE_TRACE_TILE(ti, 2);
       }
+      if (!ok) drain_loads(full, S, stage, phase, issued, wait_ns);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -500,23 +544,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       int buf = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += nunits) {
+      int ti = 0, seen = 0;
+      for (int t = unit; t < total && ok; t += nunits, ++ti) {
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int K = tb.K[tl.slot];
         const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
         bool free_acc;
-        if constexpr (CG == 2) free_acc = mbar_wait_cluster(&acc_empty[buf], acc_phase ^ 1, &abort_flag);
-        else free_acc = mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag);
+        if constexpr (CG == 2) free_acc = mbar_wait_cluster(&acc_empty[buf], acc_phase ^ 1, &abort_flag, wait_ns);
+        else free_acc = mbar_wait(&acc_empty[buf], acc_phase ^ 1, &abort_flag, wait_ns);
         if (!free_acc) break;
         tc_fence_after();
+        MOE_TRACE_TILE(ti, 3);
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN_MAX);
         if (tl.p == 0)
-          ok = mma_tile<CFG0, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, d_tmem,
-                                     K, nkb, stage, phase);
+          ok = mma_tile<CFG0, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, wait_ns, d_tmem,
+                                     K, nkb, stage, phase, seen);
         else
-          ok = mma_tile<CFG1, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, d_tmem,
-                                     K, nkb, stage, phase);
+          ok = mma_tile<CFG1, T, CG>(ring, SB, S, full, peer_full, empty, &abort_flag, wait_ns, d_tmem,
+                                     K, nkb, stage, phase, seen);
         if (!ok) break;
+        MOE_TRACE_TILE(ti, 4);
         if constexpr (CG == 2) {
           if (nkb > 0) {
             tc_commit_pair(&acc_full[buf]);
@@ -533,21 +580,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Make sure no MMA is still in flight before TMEM is released.
       tc_commit<CG>(drain);
-      mbar_wait(drain, 0, &abort_flag);
+      mbar_wait(drain, 0, &no_abort, wait_ns);
     } else if (CG == 2 && lane == 0) {
       // odd CTA of a pair: tell the even CTA's MMA issuer when each of this
       // CTA's stages has landed
-      int stage = 0;
+      int stage = 0, seen = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int t = unit; t < total && ok; t += nunits) {
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int nkb = (tb.K[tl.slot] + Elem<T>::BKE - 1) / Elem<T>::BKE;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, &abort_flag)) {
+          if (!mbar_wait(&full[stage], phase, &abort_flag, wait_ns)) {
             ok = false;
             break;
           }
+          MOE_TRACE_KB(seen, 1);
+          ++seen;
           mbar_arrive_remote(&peer_full[stage], 0);
           if (++stage == S) {
             stage = 0;
@@ -576,6 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stg_base = sEpi + q * 8192;
     uint64_t* ldb = epi_ld + q * 2;
     uint32_t ld_phase = 0;  // bit i: parity of the next wait on ldb[i]
+    uint32_t ld_pending = 0;  // bit i: a load into staging slab i not yet waited for
     int nbuf = 0;           // staging slab the next write goes to
     int buf = 0;
     uint32_t acc_phase = 0;
@@ -585,7 +635,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4));
     };
     bool ok = true;
-    for (int t = unit; t < total && ok; t += nunits) {
+    int ti = 0;
+    for (int t = unit; t < total && ok; t += nunits, ++ti) {
       const Tile tl = decode_tile<BMT>(tb, P, nge, t);
       const Problem& pr = P.pr[tl.p];
       const GroupedGemmDesc& g = pr.g;
@@ -612,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&ldb[b], 32 * 128);
           tma_load_2d(stg_base + b * 4096, tmX, &ldb[b], gcol0 + s, static_cast<int>(grow0));
         }
+        ld_pending |= 1u << b;
       };
       if (dact) {
         // every earlier store has finished reading both staging slabs
@@ -620,8 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         nbuf = 0;
         if (rows_ok > 0) fetch_aux(0, 0);  // overlaps the wait for the accumulator
       }
-      if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag)) break;
+      if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag, wait_ns)) break;
       tc_fence_after();
+      if (warp == 2 && lane == 0) MOE_TRACE_TILE(ti, 5);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              static_cast<uint32_t>(buf * BN_MAX);
       // store the staged slab: TMA for full slabs, lanes for ragged ones
@@ -713,11 +766,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (dact) {
           const int b = (s / SLAB) & 1;
           uint8_t* stg = stg_base + b * 4096;
-          if (!mbar_wait(&ldb[b], (ld_phase >> b) & 1, &abort_flag)) {
+          if (!mbar_wait(&ldb[b], (ld_phase >> b) & 1, &abort_flag, wait_ns)) {
             ok = false;
             break;
           }
           ld_phase ^= 1u << b;
+          ld_pending &= ~(1u << b);
           if (s + SLAB < ncols) {
             // prefetch the next aux slab into the other staging slab (its
             // previous store, if any, must have finished reading it)
@@ -759,6 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
+      if (warp == 2 && lane == 0) MOE_TRACE_TILE(ti, 6);
       if (lane == 0) {
         if (rank == 0) mbar_arrive(&acc_empty[buf]);
         else mbar_arrive_remote(&acc_empty[buf], 0);
@@ -778,12 +833,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
+    // after an abort: loads into the staging slabs must land before exit
+    if (lane == 0)
+      for (int b = 0; b < 2; ++b)
+        if (ld_pending & (1u << b)) mbar_wait(&ldb[b], (ld_phase >> b) & 1, &no_abort, wait_ns);
     // stores must be complete (not only done reading smem) before exit
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) MOE_TRACE_AT(2);
   // neither CTA of a pair leaves (or frees TMEM) while the other may still
   // use its shared memory or tensor memory
   if constexpr (CG == 2) cluster_sync();
@@ -844,6 +904,7 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
   auto kern = grouped_gemm_kernel<T, C0, C1, CG>;
   static bool attr_set[64] = {};   // per device
   static int max_pairs[64] = {};   // co-resident 2-CTA clusters, per device
+  static std::mutex attr_mu;       // callers may be on several host threads
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return kStatusCuda;
@@ -862,6 +923,7 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = CG == 2 ? 2 : 1;
+  std::unique_lock<std::mutex> lock(attr_mu);
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax) !=
             cudaSuccess ||
@@ -877,9 +939,11 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
     }
     attr_set[dev] = true;
   }
+  const int pairs = max_pairs[dev];
+  lock.unlock();
   if (CG == 2) {
     grid = (grid / 2) * 2;
-    if (grid > 2 * max_pairs[dev] || grid <= 0) grid = 2 * max_pairs[dev];
+    if (grid > 2 * pairs || grid <= 0) grid = 2 * pairs;
   }
   cfg.gridDim = dim3(grid);
   if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return kStatusCuda;
@@ -930,13 +994,21 @@ int launch_pair(int c0, int c1, const MultiParams& P, int grid, cudaStream_t st)
 
 }  // namespace
 
+static std::atomic<unsigned long long> g_wait_ns{MOE_WAIT_NS};
+
+unsigned long long set_wait_ns(unsigned long long ns) {
+  return g_wait_ns.exchange(ns == 0 ? MOE_WAIT_NS : ns);
+}
+
 int num_sms() {
-  static int n = 0;
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
   if (n == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    cached.store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -978,6 +1050,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   if (n <= 0 || n > kMaxProblems) return kStatusBadArg;
   MultiParams P;
   memset(&P, 0, sizeof(P));
+  P.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   int bn_max = 128, grid = 0, used = 0;
   // CTA pairs (256-row tiles) only when every problem of the launch asks
   int cg = 2;
@@ -1041,6 +1114,9 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   P.nprob = used;
   if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0) grid = num_sms();
+#ifdef MOE_TRACE
+  if (const char* g = getenv("MOE_TRACE_GRID")) grid = atoi(g);  // timeline experiments only
+#endif
   const int c0 = cfg_of(P.pr[0].a_mn, P.pr[0].b_mn, P.pr[0].bn, P.pr[0].epi == EPI_SWIGLU);
   const int c1 = used > 1 ? cfg_of(P.pr[1].a_mn, P.pr[1].b_mn, P.pr[1].bn,
                                    P.pr[1].epi == EPI_SWIGLU)
@@ -1072,3 +1148,17 @@ int run_grouped_gemm(const GemmOperands& op, const GroupedGemmDesc& g, int epi, 
 }
 
 }  // namespace moe
+
+#ifdef MOE_TRACE
+// Copy the per-CTA timeline of the last traced launch (two [160][64] uint64
+// arrays of ns stamps, zero where no event was recorded) and clear it.
+extern "C" __attribute__((visibility("default"))) int moe_trace_read(unsigned long long* host) {
+  if (cudaMemcpyFromSymbol(host, moe::g_trace, sizeof(moe::g_trace)) != cudaSuccess) return -3;
+  if (cudaMemcpyFromSymbol(host + moe::kTraceCtas * moe::kTraceSlots, moe::g_trace_kb,
+                           sizeof(moe::g_trace_kb)) != cudaSuccess)
+    return -3;
+  static unsigned long long zeros[moe::kTraceCtas * moe::kTraceSlots] = {};
+  if (cudaMemcpyToSymbol(moe::g_trace_kb, zeros, sizeof(zeros)) != cudaSuccess) return -3;
+  return cudaMemcpyToSymbol(moe::g_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : -3;
+}
+#endif

@@ -40,4 +40,8 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
 
 int num_sms();
 
+// Limit (ns) of the grouped GEMM's device-side waits for launches that follow;
+// 0 restores the default.  Returns the previous limit.
+unsigned long long set_wait_ns(unsigned long long ns);
+
 }  // namespace moe

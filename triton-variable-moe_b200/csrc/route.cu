@@ -425,14 +425,22 @@ template <typename S>
 static int route_impl(const S* sel, long long A, int E, int bs, int mode, const RouteOut& o,
                       void* ws, long long ws_bytes, cudaStream_t st) {
   if (A <= kSmallMaxA) {
+    // the kernel's shared-memory limit, raised once per device (callers may be
+    // on several host threads)
     static bool attr_set[64] = {};
+    static std::mutex attr_mu;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-      if (cudaFuncSetAttribute(route_small_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kSmallMaxA * 2)) != cudaSuccess)
-        return kStatusCuda;
-      attr_set[dev] = true;
+    if (dev < 0 || dev >= 64) return kStatusCuda;
+    {
+      std::lock_guard<std::mutex> lock(attr_mu);
+      if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(route_small_kernel<S>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmallMaxA * 2)) != cudaSuccess)
+          return kStatusCuda;
+        attr_set[dev] = true;
+      }
     }
     const int rc = launch_pdl(route_small_kernel<S>, 1, kSmallWarps * 32,
                               static_cast<int>(A * 2), st, sel, A, E, bs, mode, o);
@@ -512,6 +520,9 @@ int route_static_scratch(const void* sel, int sel_is_int64, long long A, int E, 
                          long long p_cap, int32_t* asg_row, int* status, cudaStream_t st) {
   if (E <= 0 || E > kMaxE || A < 0) return kStatusBadArg;
   const long long need = route_workspace_bytes(A, E);
+  // unit_size() keeps the unit count <= 256 and E <= kMaxE was checked above,
+  // so `need` never exceeds the array today (256 units x kMaxE ints); the check
+  // stays as a guard should either bound change
   if (need > kRouteScratchInts * 4) return kStatusCapacity;
   int err = kStatusOk;
   void* ws = route_scratch_address(&err);

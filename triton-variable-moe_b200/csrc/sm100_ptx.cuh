@@ -10,6 +10,8 @@
 #ifndef MOE_WAIT_NS
 #define MOE_WAIT_NS 2000000000ull  // 2 s: far beyond any legitimate wait
 #endif
+// Callers pass their own limit (the grouped GEMM takes it from its launch
+// parameters, settable at run time); MOE_WAIT_NS is the default.
 
 namespace moe {
 
@@ -65,14 +67,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait on the phase with the given parity.  Returns false when the
 // wait gave up (timeout or another role raised the CTA abort flag).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          uint64_t limit_ns = MOE_WAIT_NS) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > MOE_WAIT_NS) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       return false;
     }
@@ -111,14 +114,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 // Bounded wait (cluster-scope acquire) for a barrier that peer CTAs arrive on.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort_flag) {
+                                                  volatile int* abort_flag,
+                                                  uint64_t limit_ns = MOE_WAIT_NS) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait_cluster(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait_cluster(a, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > MOE_WAIT_NS) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       return false;
     }

@@ -39,6 +39,7 @@ _L = c_int64
 # name -> argtypes (all functions return int unless listed in _RESTYPE)
 _SIGS = {
     "moe_version": [],
+    "moe_set_wait_timeout_ns": [ctypes.c_uint64],
     "moe_status_string": [_I],
     "moe_route_workspace_bytes": [_L, _I],
     "moe_route": [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _P, _P],
@@ -77,6 +78,7 @@ _SIGS = {
 }
 _RESTYPE = {
     "moe_version": c_char_p,
+    "moe_set_wait_timeout_ns": ctypes.c_uint64,
     "moe_status_string": c_char_p,
     "moe_route_workspace_bytes": c_int64,
     "moe_router_head_workspace_floats": c_int64,

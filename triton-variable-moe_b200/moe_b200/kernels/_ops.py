@@ -94,6 +94,8 @@ def check_device_status(device: torch.device | None = None) -> None:
     v = int(buf.item())
     if v != 0:
         buf.zero_()
+        # a launch that gave up may have left its row-block counters non-zero
+        reset_up_down_dep_buffer(device)
         raise MoEKernelError(f"device-side error: {STATUS_TEXT.get(v, v)} (status {v})")
 
 
@@ -447,6 +449,17 @@ def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> tor
     return buf
 
 
+def reset_up_down_dep_buffer(device: torch.device) -> None:
+    """Zero the device's gemm_up_down counters (stream-ordered).  Every launch
+    that completes normally leaves them at zero; one that gave up (a device
+    wait ran out, status MOE_ERR_TIMEOUT) may not, and a later launch could
+    then pass its waits too early."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _dep_buffers.get(torch.device("cuda", idx))
+    if buf is not None:
+        buf.zero_()
+
+
 def gemm_up_down(x, w1, w2, tok_off, w_off, tok_cnt, num_experts, inter, pre_act, out,
                  tile_n_width=0, tile_n_hidden=0):
     """inter = relu(x @ w1_e)^2 (pre_act = relu(x @ w1_e)), out = inter @ w2_e in
@@ -463,6 +476,8 @@ def gemm_up_down(x, w1, w2, tok_off, w_off, tok_cnt, num_experts, inter, pre_act
         int(tile_n_hidden), ptr(status_buffer(x.device)), stream_handle(x.device),
     )
     _ev_end(ev, "grouped_gemm_up_down")
+    if rc != 0:
+        reset_up_down_dep_buffer(x.device)
     check(rc, "moe_grouped_gemm_up_down")
     _count(1)
     return out

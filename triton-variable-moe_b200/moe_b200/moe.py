@@ -270,36 +270,16 @@ class TritonMoEMLP(nn.Module):
             if count > 1:
                 group_sizes.append(count)
                 gidx += 1
-        self._num_valid_groups = len(group_sizes)
-        self._all_experts_valid = all(g >= 0 for g in expert_to_group)
-        if self._num_valid_groups > 0:
-            membership = torch.zeros(self.num_experts, self._num_valid_groups)
-            for i, g in enumerate(expert_to_group):
-                if g >= 0:
-                    membership[i, g] = 1.0
-            self.register_buffer("group_membership", membership, persistent=False)
-            self.register_buffer("group_sizes", torch.tensor(group_sizes, dtype=torch.float32),
-                                 persistent=False)
-            self.register_buffer(
-                "valid_expert_indices",
-                torch.tensor([i for i, g in enumerate(expert_to_group) if g >= 0],
-                             dtype=torch.long),
-                persistent=False,
-            )
-        else:
-            self.register_buffer("group_membership", torch.empty(0), persistent=False)
-            self.register_buffer("group_sizes", torch.tensor([1.0]), persistent=False)
-            self.register_buffer("valid_expert_indices", torch.empty(0, dtype=torch.long),
-                                 persistent=False)
+        num_groups = len(group_sizes)
         # load_balance_loss = sum_e lb_coef[e] * f_i[e] * p_i[e]: the three cases of
         # moe.py:276-303 (uniform widths, no size group with >1 expert, groups)
         if len(set(self.expert_widths)) == 1:
             coef = [float(self.num_experts)] * self.num_experts
-        elif self._num_valid_groups == 0:
+        elif num_groups == 0:
             coef = [1.0] * self.num_experts
         else:
             coef = [
-                (group_sizes[g] / self._num_valid_groups) if g >= 0 else 0.0
+                (group_sizes[g] / num_groups) if g >= 0 else 0.0
                 for g in expert_to_group
             ]
         # kept out of the module's buffers so that module.to(dtype) does not round it
@@ -375,20 +355,6 @@ class TritonMoEMLP(nn.Module):
         aux = {"router_z_loss": z, "load_balance_loss": lb, "compute_loss": cl}
         return aux, f_i
 
-    def _aux_losses_reference(self, router_logits, router_probs, tokens_per_expert, dtype):
-        """The reference's torch expressions of the auxiliary losses (moe.py:253-272);
-        used as the checker of the fused kernels."""
-        router_z_loss = torch.logsumexp(router_logits, dim=-1).pow(2).mean()
-        f_i = (tokens_per_expert.float() / tokens_per_expert.sum()).to(dtype)
-        load_balance_loss = self._compute_load_balance_loss(router_probs, f_i)
-        compute_loss = (router_probs @ self.expert_widths_normalized.to(router_probs.dtype)).mean()
-        aux = {
-            "router_z_loss": router_z_loss,
-            "load_balance_loss": load_balance_loss,
-            "compute_loss": compute_loss,
-        }
-        return aux, f_i
-
     # ------------------------------------------------------------------ forward
     @torch.compiler.disable
     def forward(self, x: torch.Tensor):
@@ -405,22 +371,6 @@ class TritonMoEMLP(nn.Module):
         self._join_aux(x.device)
         aux, f_i = self._aux_losses(router_logits, lse, head_losses, router_probs)
         return output, aux, f_i
-
-    def _compute_load_balance_loss(self, router_probs: torch.Tensor, f_i: torch.Tensor) -> torch.Tensor:
-        """Load-balance loss within expert size groups (moe.py:276-303)."""
-        p_i = router_probs.mean(dim=0)
-        if len(set(self.expert_widths)) == 1:
-            return self.num_experts * (f_i.float() @ p_i.float())
-        if self._num_valid_groups == 0:
-            return f_i.float() @ p_i.float()
-        fi_pi = f_i.float() * p_i.float()
-        membership = self.group_membership.to(fi_pi.dtype)
-        if self._all_experts_valid:
-            group_sums = fi_pi @ membership
-        else:
-            group_sums = fi_pi.index_select(0, self.valid_expert_indices) @ membership.index_select(
-                0, self.valid_expert_indices)
-        return (self.group_sizes.to(fi_pi.dtype) * group_sums).mean()
 
     def _offsets(self, padded_bins, device):
         expert_token_offsets = torch.cat(
