@@ -16,20 +16,21 @@ __device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
 // issued the loads, [32, 64) the MMA issuer (or a pair's relay) saw them land
 __device__ unsigned long long g_trace_kb[kTraceCtas * kTraceSlots];
 }  // namespace moe
-#define MOE_TRACE_KB(j, ev)                                                               \
-  do {                                                                                    \
-    if (blockIdx.x < moe::kTraceCtas && (j) < 32)                                         \
-      moe::g_trace_kb[blockIdx.x * moe::kTraceSlots + (ev) * 32 + (j)] = moe::global_timer_ns(); \
-  } while (0)
 #define MOE_TRACE_AT(slot)                                                                  \
   do {                                                                                      \
     if (blockIdx.x < moe::kTraceCtas && (slot) < moe::kTraceSlots)                          \
       moe::g_trace[blockIdx.x * moe::kTraceSlots + (slot)] = moe::global_timer_ns();       \
   } while (0)
 // per-tile event `ev` (0..6) of the CTA's `i`-th tile (first 8 tiles only)
-#define MOE_TRACE_TILE(i, ev)                  \
-  do {                                         \
+#define MOE_TRACE_TILE(i, ev)                      \
+  do {                                             \
     if ((i) < 8) MOE_TRACE_AT(3 + (i) * 7 + (ev)); \
+  } while (0)
+#define MOE_TRACE_KB(j, ev)                                                                \
+  do {                                                                                     \
+    if (blockIdx.x < moe::kTraceCtas && (j) < 32)                                          \
+      moe::g_trace_kb[blockIdx.x * moe::kTraceSlots + (ev) * 32 + (j)] =                  \
+          moe::global_timer_ns();                                                          \
   } while (0)
 #else
 #define MOE_TRACE_AT(slot) \
