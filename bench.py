@@ -34,8 +34,8 @@ Extra keys:
                    and permutation rooflines
   route_roofline   routing alone at A = 131072 and 524288 assignments (N=1)
   ep_c5            the 4096-hidden 128-expert top-8 layer with its experts
-                   sharded over the N GPUs (NCCL all-to-all dispatch and
-                   combine; at N=1 a one-rank group): tokens/s, GEMM roofline,
+                   sharded over the N GPUs (dispatch and combine kernels over
+                   NVLink peer memory; at N=1 a one-rank group): tokens/s, GEMM roofline,
                    and an in-run parity check of every rank's output and dX
                    against the unsharded layer on a token slice
   cpu_baseline     the reference's own kernels (triton_moe from baseline/_ref)
@@ -526,22 +526,21 @@ def capture_step(layer, x, gout, kernel_events=False):
 
     from moe_b200.kernels import _ops
 
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            layer.zero_grad(set_to_none=True)
-            x.grad = None
-            out, _, _ = layer(x)
-            out.backward(gout)
-    torch.cuda.current_stream().wait_stream(s)
+    # warm-up and capture on the caller's (non-default) stream: the autograd
+    # nodes that accumulate into the long-lived leaves (x, the parameters) then
+    # always run on the stream they were created on
+    for _ in range(3):
+        layer.zero_grad(set_to_none=True)
+        x.grad = None
+        out, _, _ = layer(x)
+        out.backward(gout)
     torch.cuda.synchronize()
     layer.zero_grad(set_to_none=True)
     x.grad = None
     graph = torch.cuda.CUDAGraph()
     l0 = _ops.launch_count
     evs: list = []
-    with torch.cuda.graph(graph):
+    with torch.cuda.graph(graph, stream=torch.cuda.current_stream()):
         if kernel_events:
             with _ops.record_kernel_events(external=True) as evs:
                 out, _, _ = layer(x)
@@ -586,7 +585,7 @@ def capture_with_gemm_graph(layer, x, gout):
             setattr(_lib.lib, n, orig[n])
     step_calls = calls[-len(GEMM_ENTRY_POINTS):]  # the captured step's launches
     gg = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gg):
+    with torch.cuda.graph(gg, stream=torch.cuda.current_stream()):
         st = torch.cuda.current_stream().cuda_stream
         for n, a in step_calls:
             rc = orig[n](*a[:-1], st)  # the stream is every entry point's last argument
@@ -738,7 +737,7 @@ def measure_route(dev, flush, steps, peaks):
         torch.cuda.synchronize()
         P = int(r.expert_token_offsets[-1].item())
         gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
+        with torch.cuda.graph(gr, stream=torch.cuda.current_stream()):
             _ops.route(sel, E, 64)
         for _ in range(3):
             gr.replay()
@@ -848,12 +847,18 @@ def run_ep_c5(args, dev, ws, rank, flush, peaks):
                      "timing": "event-timed grouped-GEMM launches of one eager step, this rank's "
                                "FLOPs; slowest rank"},
         "kernel_ms_per_step_rank0": {k: round(v, 3) for k, v in sorted(per_kind.items())},
-        "exchange": "NCCL all_to_all_single (4 row exchanges per step, not overlapped)",
+        "exchange": ("fused dispatch (gather + NVLink push into the owners' layouts) and "
+                     "combine (NVLink pull + weighted sum) kernels on an exchange stream, "
+                     "token chunks pipelined against the grouped GEMMs, NCCL barriers"),
     }
-    if ws == 1:
-        res["permute_roofline"] = permute_roofline(
-            permute_bytes(cfg), sum(v for k, v in per_kind.items()
-                                    if k in ("gather", "weighted_gather", "combine")), peaks[1])
+    perm_ms = sum(v for k, v in per_kind.items() if k in ("ep_dispatch", "ep_combine"))
+    if ws == 1 and perm_ms > 0:
+        # at one rank the fused exchange kernels move the same bytes as the
+        # single-GPU gather / combine kernels, all through local HBM
+        res["permute_roofline"] = permute_roofline(permute_bytes(cfg), perm_ms, peaks[1])
+        res["permute_roofline"]["kernels"] = ("ep_dispatch (gather fused with the push) and "
+                                              "ep_combine (pull fused with the weighted sum), "
+                                              "forward and backward")
     del layer
     torch.cuda.empty_cache()
     return res
@@ -897,6 +902,8 @@ def run_b200(args, cfg, name):
         return 1
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # every step (eager, captured, replayed) runs on one non-default stream
+    torch.cuda.set_stream(torch.cuda.Stream(device=dev))
     timeout = datetime.timedelta(minutes=10)
     if ws > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=timeout)

@@ -41,12 +41,16 @@ extern "C" {
 #define MOE_ERR_TIMEOUT (-4)
 #define MOE_ERR_CAPACITY (-5)
 #define MOE_ERR_BAD_EXPERT (-6)
+#define MOE_ERR_COMM (-7) /* NCCL missing or an NCCL call failed */
 
 #define MOE_DTYPE_BF16 0
 #define MOE_DTYPE_F16 1
 #define MOE_DTYPE_F32 2
 
 #define MOE_TILE_PAIR 0x200 /* tile_n flag: 256-row tiles on SM pairs */
+/* tile_n field: run the launch on at most n persistent CTAs (0 = one per SM),
+ * e.g. to leave SMs to communication kernels running alongside */
+#define MOE_TILE_CTAS(n) ((n) << 16)
 
 #define MOE_ACT_NONE 0
 #define MOE_ACT_RELU_SQUARED 1
@@ -237,7 +241,8 @@ MOE_API int moe_relu_squared_grad(const void* grad_out, const void* pre_act, int
  *   rows                  rows of the token-space operands (allocation size)
  *   tile_n                N tile 128 or 256 (0 = choose); OR MOE_TILE_PAIR for
  *                         256-row tiles computed by SM pairs (2-CTA clusters,
- *                         cta_group::2 MMAs) instead of 128-row tiles
+ *                         cta_group::2 MMAs) instead of 128-row tiles; OR
+ *                         MOE_TILE_CTAS(n) to cap the persistent grid at n CTAs
  * Every expert width and every expert row count used as a reduction length
  * must be a multiple of 16; H must be a multiple of 16.
  */
@@ -364,6 +369,112 @@ MOE_API int moe_grouped_gemm_up_backward(
     const int32_t* expert_weight_offsets, const int32_t* tokens_per_expert, int num_experts,
     void* grad_x, int64_t ld_grad_x, void* grad_w1, int dtype, int tile_n_width,
     int tile_n_hidden, int* status, void* stream);
+
+/*
+ * Expert parallelism (EP): the token exchange between the ranks that share
+ * one layer's experts.  The reference runs the layer on one GPU
+ * (triton_moe/moe.py:185-249: gather -> grouped GEMMs -> scatter); sharded,
+ * each rank routes its own tokens (moe_route with block size 1: its rows in
+ * expert-sorted order), and
+ *   moe_ep_dispatch  (the gather, fused with the transfer) pushes each row
+ *                    straight into the padded expert-contiguous layout of
+ *                    the expert's owner (the rows the owner's grouped GEMMs
+ *                    read), in the owner's memory;
+ *   moe_ep_combine   (the scatter, fused with the transfer) forms each
+ *                    token's top-k sum from the owners' output rows, read
+ *                    from the owners' memory.
+ * Owners' layouts live in buffers made with moe_ep_buffer_create and mapped
+ * on every rank with moe_ep_buffer_open (CUDA IPC over NVLink); `peers` is a
+ * device array of the world's base pointers of one such buffer (this rank's
+ * own entry may be its local pointer).  Ranks order their accesses to each
+ * other's buffers with moe_ep_barrier on the streams that access them: after
+ * the last read of a buffer and before the next write into it, and after the
+ * writes and before the reads.
+ *
+ * Conventions: `owner` is the rank that owns each global expert (host int32
+ * for moe_ep_plan, a device copy for the kernels); a rank's local experts are
+ * the ids it owns, ascending.  `counts` (host, int32,
+ * [world][chunks][num_experts] row-major) holds how many rows every source
+ * rank sends to each expert in each chunk (tokens split into chunks that are
+ * exchanged one after another, so that one chunk's GEMMs overlap another's
+ * transfers): every rank gathers it with moe_ep_gather_counts.  `comm` is an
+ * ncclComm_t of the world's ranks (moe_ep_comm_init, or the caller's own);
+ * NCCL is loaded at run time (libnccl.so.2, the copy already in the process
+ * if there is one).  Every collective call on a communicator must be made by
+ * all its ranks in the same order.
+ */
+
+/* ncclGetUniqueId: 128 bytes for moe_ep_comm_init, made on one rank and sent
+ * to the others by the caller's own means. */
+MOE_API int moe_ep_unique_id(void* id);
+/* ncclCommInitRank on the current CUDA device; collective over the ranks. */
+MOE_API int moe_ep_comm_init(void** comm, const void* id, int world, int rank);
+MOE_API int moe_ep_comm_destroy(void* comm);
+
+/* All-gather of every rank's `n` int32 counts (device buffers; `all` holds
+ * world * n, in rank order). */
+MOE_API int moe_ep_gather_counts(void* comm, const int32_t* mine, int32_t* all, int64_t n,
+                                 void* stream);
+
+/* Stream-ordered barrier of the communicator's ranks (an all-reduce of one
+ * int32 device word; its value is not meaningful). */
+MOE_API int moe_ep_barrier(void* comm, int32_t* word, void* stream);
+
+/* Device buffers other ranks can map: cudaMalloc + a 64-byte CUDA IPC
+ * handle; moe_ep_buffer_open maps a peer's handle (peer access enabled on
+ * first use), moe_ep_buffer_close unmaps it. */
+MOE_API int moe_ep_buffer_create(int64_t bytes, void** ptr, void* ipc_handle);
+MOE_API int moe_ep_buffer_free(void* ptr);
+MOE_API int moe_ep_buffer_open(const void* ipc_handle, void** ptr);
+MOE_API int moe_ep_buffer_close(void* ptr);
+
+/* Host-side plan of the exchange from the gathered counts (no device work).
+ * The owner's layout has one region per local expert; a region holds one
+ * block per chunk, each with the sources' rows in rank order, rounded up to
+ * block_size rows.
+ *   src_off    [chunks][num_experts]: first row of (chunk, expert) in this
+ *              rank's expert-sorted rows of that chunk
+ *   tok_off    [E_local + 1]: the regions (expert_token_offsets of the whole
+ *              layout: the weight-gradient GEMMs reduce over all chunks)
+ *   chunk_off  [chunks][E_local + 1]: first row of each chunk's block in each
+ *              region, last entry = total rows (expert_token_offsets of one
+ *              chunk's GEMMs, with chunk_rows as their tokens_per_expert)
+ *   chunk_rows [chunks][E_local]: rows of each chunk's block (padded)
+ *   recv_off   [world][chunks][E_local]: first row of the block from each
+ *              source rank
+ * The row of this rank's expert-sorted row i of chunk c (expert e) in its
+ * owner's layout is i - src_off[c][e] + the owner's recv_off[rank][c][e's
+ * local index]: the `delta` of moe_ep_dispatch / moe_ep_combine.  Padding
+ * rows (past a block's received rows) are not written by the exchange;
+ * callers zero them. */
+MOE_API int moe_ep_plan(int world, int rank, int chunks, int num_experts, int block_size,
+                        const int32_t* owner, const int32_t* counts, int64_t* src_off,
+                        int32_t* tok_off, int32_t* chunk_off, int32_t* chunk_rows,
+                        int64_t* recv_off);
+
+/* Dispatch one chunk: row i < rows of this rank's expert-sorted rows
+ * (row_to_assignment[i] = t * top_k + j, expert bin_ids[i], from moe_route
+ * with block size 1 over the chunk's assignments) is token t of x (times
+ * weights[row_to_assignment[i]] when weights is not NULL, rounded to the
+ * storage type: the weighted gather of the backward) and is stored at row
+ * i + delta[e] of peers[owner[e]] (row stride ld_peer).  owner [E] int32,
+ * delta [E] int64 and peers [world] are device arrays. */
+MOE_API int moe_ep_dispatch(const void* x, int64_t ld_x, int64_t hidden,
+                            const int32_t* row_to_assignment, int top_k, const void* weights,
+                            const int32_t* bin_ids, int64_t rows, const int32_t* owner,
+                            const int64_t* delta, void* const* peers, int64_t ld_peer,
+                            int dtype, void* stream);
+
+/* Combine one chunk: out[t] = sum_j round(Y(t, j) * weights[t*top_k + j])
+ * (unit weights when NULL), summed in fp32 and rounded once, for t <
+ * num_tokens, where assignment a = t*top_k + j is at expert-sorted row
+ * r = assignment_to_row[a], its expert is e = bin_ids[r] and Y(t, j) is row
+ * r + delta[e] of peers[owner[e]]. */
+MOE_API int moe_ep_combine(void* const* peers, int64_t ld_peer, const int32_t* owner,
+                           const int64_t* delta, const int32_t* bin_ids,
+                           const int32_t* assignment_to_row, int64_t num_tokens, int top_k,
+                           const void* weights, int64_t hidden, void* out, int64_t ld_out,
+                           int dtype, void* stream);
 
 #ifdef __cplusplus
 }

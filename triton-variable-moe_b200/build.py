@@ -23,7 +23,7 @@ INCLUDE = HERE.parent / "include"
 OBJ_DIR = HERE / "_build"
 OUT = HERE / "moe_b200" / "libmoe_b200.so"
 
-SOURCES = ["route.cu", "router.cu", "permute.cu", "grouped_gemm.cu", "capi.cu"]
+SOURCES = ["route.cu", "router.cu", "permute.cu", "grouped_gemm.cu", "capi.cu", "ep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",
@@ -76,7 +76,8 @@ def build(force: bool = False, jobs: int = 4, verbose_ptxas: bool = False,
         list(ex.map(lambda so: _compile(so[0], so[1], extra), todo))
     if todo or force or not out.exists():
         # exported symbols: only the extern "C" ABI (default visibility below)
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(out), *map(str, objs), "-Xcompiler", "-fPIC"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(out), *map(str, objs), "-Xcompiler", "-fPIC",
+               "-ldl"]
         subprocess.run(cmd, check=True)
     return out
 

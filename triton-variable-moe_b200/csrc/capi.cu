@@ -60,12 +60,14 @@ bool gemm_dtype_ok(int dtype) {
 }
 
 int pick_bn(int tile_n, long long n_hint) {
-  const int t = tile_n & ~MOE_TILE_PAIR;
+  const int t = tile_n & 0x1FF;
   if (t == 128 || t == 256) return t;
   return (n_hint > 0 && n_hint % 256 == 0) ? 256 : 128;
 }
 // 2: 256-row tiles on 2-CTA clusters; 1: 128-row tiles on single CTAs.
 int pick_pair(int tile_n) { return (tile_n & MOE_TILE_PAIR) ? 2 : 1; }
+// MOE_TILE_CTAS(n): run the launch on at most n CTAs (0: one per SM).
+int pick_ctas(int tile_n) { return (tile_n >> 16) & 0x7FFF; }
 
 GroupedGemmDesc base_desc(const int32_t* tok_off, const int32_t* tok_cnt, const int32_t* w_off,
                           int E, long long hidden, int* status) {
@@ -104,6 +106,7 @@ const char* moe_status_string(int s) {
     case MOE_ERR_TIMEOUT: return "device-side wait timed out";
     case MOE_ERR_CAPACITY: return "padded row capacity exceeded";
     case MOE_ERR_BAD_EXPERT: return "expert id out of range";
+    case MOE_ERR_COMM: return "NCCL unavailable or an NCCL call failed";
     default: return "unknown status";
   }
 }
@@ -277,6 +280,7 @@ Built build_up(const void* x, int64_t rows, int64_t ld_x, const void* w1, int64_
   b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
                       pick_bn(tile_n, 0), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -311,6 +315,7 @@ Built build_up_swiglu(const void* x, int64_t rows, int64_t ld_x, const void* w1,
   b.op = GemmOperands{x, rows, hidden, ld_x, 0, w1, hidden, total_width, total_width, 1,
                       pick_bn(tile_n, 0), 0};
   b.op.pair = 1;
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -336,6 +341,7 @@ Built build_down(const void* inter, int64_t rows, int64_t ld_inter, const void* 
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 0, w2, total_width, hidden, hidden, 1,
                       pick_bn(tile_n, hidden), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -362,6 +368,7 @@ Built build_up_dx(const void* grad_act, int64_t rows, int64_t ld_ga, const void*
   b.op = GemmOperands{grad_act, rows, ld_ga, ld_ga, 0, w1, hidden, total_width, total_width, 0,
                       pick_bn(tile_n, hidden), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -386,6 +393,7 @@ Built build_up_dw(const void* x, int64_t rows, int64_t ld_x, const void* grad_ac
   b.op = GemmOperands{x, rows, hidden, ld_x, 1, grad_act, rows, ld_ga, ld_ga, 1,
                       pick_bn(tile_n, 0), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -416,6 +424,7 @@ Built build_down_dinter(const void* grad_y, int64_t rows, int64_t ld_gy, const v
   b.op = GemmOperands{grad_y, rows, hidden, ld_gy, 0, w2, total_width, hidden, hidden, 0,
                       pick_bn(tile_n, 0), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 
@@ -440,6 +449,7 @@ Built build_down_dw(const void* inter, int64_t rows, int64_t ld_inter, const voi
   b.op = GemmOperands{inter, rows, ld_inter, ld_inter, 1, grad_y, rows, hidden, ld_gy, 1,
                       pick_bn(tile_n, hidden), 0};
   b.op.pair = pick_pair(tile_n);
+  b.op.grid = pick_ctas(tile_n);
   return b;
 }
 

@@ -1113,7 +1113,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   if (used == 0) return kStatusOk;
   P.nprob = used;
   if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
-  if (grid <= 0) grid = num_sms();
+  if (grid <= 0 || grid > num_sms()) grid = num_sms();
 #ifdef MOE_TRACE
   if (const char* g = getenv("MOE_TRACE_GRID")) grid = atoi(g);  // timeline experiments only
 #endif

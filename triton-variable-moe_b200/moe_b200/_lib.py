@@ -25,12 +25,18 @@ STATUS_TEXT = {
     -4: "device-side wait timed out",
     -5: "padded row capacity exceeded",
     -6: "expert id out of range",
+    -7: "NCCL unavailable or an NCCL call failed",
 }
 
 DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 ACT_CODE = {"none": 0, "relu_squared": 1, "swiglu": 2}
 ROUND_CODE = {"up": 0, "down": 1, "nearest": 2}
 TILE_PAIR = 0x200  # tile_n flag: 256-row tiles on SM pairs (2-CTA clusters)
+
+
+def tile_ctas(n: int) -> int:
+    """tile_n field capping the persistent GEMM grid at n CTAs (MOE_TILE_CTAS)."""
+    return int(n) << 16
 
 _P = c_void_p
 _I = c_int
@@ -75,6 +81,18 @@ _SIGS = {
         _P, _L, _L, _P, _L, _P, _L, _L, _P, _P, _P, _I, _P, _L, _P, _I, _I, _I, _P, _P,
     ],
     "moe_grouped_gemm_down_dw": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _I, _P, _I, _I, _P, _P],
+    "moe_ep_unique_id": [_P],
+    "moe_ep_comm_init": [_P, _P, _I, _I],
+    "moe_ep_comm_destroy": [_P],
+    "moe_ep_gather_counts": [_P, _P, _P, _L, _P],
+    "moe_ep_barrier": [_P, _P, _P],
+    "moe_ep_buffer_create": [_L, _P, _P],
+    "moe_ep_buffer_free": [_P],
+    "moe_ep_buffer_open": [_P, _P],
+    "moe_ep_buffer_close": [_P],
+    "moe_ep_plan": [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    "moe_ep_dispatch": [_P, _L, _L, _P, _I, _P, _P, _L, _P, _P, _P, _L, _I, _P],
+    "moe_ep_combine": [_P, _L, _P, _P, _P, _P, _L, _I, _P, _L, _P, _L, _I, _P],
 }
 _RESTYPE = {
     "moe_version": c_char_p,
