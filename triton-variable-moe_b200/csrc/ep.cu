@@ -223,11 +223,11 @@ __global__ void __launch_bounds__(kEpThreads)
 // bin_ids[asg_row[a]], and its output row is asg_row[a] + delta[e] of the
 // owner's layout, read from the owner's memory (peers[owner[e]]).  One warp
 // per token; every source row's vectors of a column pass are loaded before
-// any is summed.  At most ~85 registers per thread.
+// any is summed.
 constexpr int kPullK = 8;   // source rows loaded together
-constexpr int kPullVec = 1;  // 16-byte vectors per lane and source row per pass
+constexpr int kPullVec = 2;  // 16-byte vectors per lane and source row per pass
 template <typename T>
-__global__ void __launch_bounds__(kEpThreads, 3)
+__global__ void __launch_bounds__(kEpThreads, 2)
     ep_pull_combine_kernel(T* const* __restrict__ peers, long long ldp,
                            const int32_t* __restrict__ owner, const long long* __restrict__ delta,
                            const int32_t* __restrict__ bin_ids, const int32_t* __restrict__ asg_row,
