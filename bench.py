@@ -85,7 +85,7 @@ REF_CPU_TOKENS = 256
 # DRAM bytes (read + write) of one c3 step's grouped-GEMM launches, summed over
 # the launches, from one ncu capture (--metrics dram__bytes_read.sum,
 # dram__bytes_write.sum; committed summary profiles/grouped_gemm_c3.md).
-NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 142918144}
+NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 144706560}
 
 
 def _pkg_path():
