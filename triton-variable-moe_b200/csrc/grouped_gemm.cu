@@ -32,11 +32,20 @@ namespace {
 
 constexpr int BM = 128;  // UMMA M: one TMEM lane per output row
 constexpr int BN_MAX = 256;
-constexpr int kThreads = 192;
+#ifndef MOE_EPI_WARPS
+#define MOE_EPI_WARPS 4
+#endif
+// Epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter, each
+// taking half of a tile's column slabs).  8 take 32 KB more staging memory, so
+// the ring has 3 stages instead of 4 at N tile 256; measured slower at the c3
+// and c4 shapes (c3 GEMM step 88 vs 82 us), hence 4.
+constexpr int kEpiWarps = MOE_EPI_WARPS;
+static_assert(kEpiWarps == 4 || kEpiWarps == 8, "4 or 8 epilogue warps");
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxStages = 8;
 constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-block
 constexpr int kSmemMax = 227 * 1024;     // dynamic shared memory per CTA on sm_100
-constexpr int kEpiBytes = 4 * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
+constexpr int kEpiBytes = kEpiWarps * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
 constexpr int kBarBytes = 512;            // mbarriers, TMEM address, abort flag
 
@@ -337,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bars + 2 * kMaxStages;
   uint64_t* acc_empty = bars + 2 * kMaxStages + 2;
   uint64_t* drain = bars + 2 * kMaxStages + 4;
-  uint64_t* epi_ld = bars + 2 * kMaxStages + 5;  // [4 warps][2 slabs]: aux tile loads
+  uint64_t* epi_ld = bars + 3 * kMaxStages + 15;  // [epilogue warps][2 slabs]: aux loads
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
   int& abort_flag = *reinterpret_cast<int*>(bars + 2 * kMaxStages + 14);
   uint64_t* peer_full = bars + 2 * kMaxStages + 15;  // [stages], even CTA of a pair
@@ -372,10 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4 * CG);  // one arrival per epilogue warp of the pair
+      mbar_init(&acc_empty[i], kEpiWarps * CG);  // one arrival per epilogue warp of the pair
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&epi_ld[i], 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&epi_ld[i], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -499,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // rows of A written by problem 0 in this launch: wait for their row block
           const int s0 = tl.slot - P.pr[0].g.E;  // the same expert in problem 0
           const int blk = tb.mtp[s0] + tl.m0 / BMT;
-          const int need = 4 * ((tb.N[s0] + P.pr[0].tile_n - 1) / P.pr[0].tile_n);
+          const int need = kEpiWarps * ((tb.N[s0] + P.pr[0].tile_n - 1) / P.pr[0].tile_n);
           if (blk >= g.dep_len) {
             if (g.status != nullptr) atomicExch(g.status, kStatusBadArg);
             abort_flag = 1;
@@ -609,7 +618,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     // Each warp owns 32 accumulator rows (its TMEM lane quarter) and produces
-    // them one slab at a time: 32 rows x 128 bytes (64 bf16 / 32 fp32 columns).
+    // them one slab at a time: 32 rows x 128 bytes (64 bf16 / 32 fp32 columns);
+    // with 8 epilogue warps two warps share a quarter, each taking half of the
+    // tile's slabs.
     // Every lane converts its own row into a shared staging slab laid out in
     // the TMA 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)), then
     // one lane stores the slab with a TMA tensor store and the warp moves on;
@@ -621,9 +632,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // into the staging slab one slab ahead and computes in place.
     constexpr int EPC = Elem<T>::EPC;  // elements per 16-byte chunk
     constexpr int SLAB = 8 * EPC;      // columns per slab
-    const int q = warp & 3;
-    uint8_t* stg_base = sEpi + q * 8192;
-    uint64_t* ldb = epi_ld + q * 2;
+    const int q = warp & 3;          // TMEM lane quarter (the hardware's warp % 4 rule)
+    const int ew = warp - 2;         // epilogue warp index
+    const int half = ew / 4;         // with 8 warps: which half of the column slabs
+    uint8_t* stg_base = sEpi + ew * 8192;
+    uint64_t* ldb = epi_ld + ew * 2;
     uint32_t ld_phase = 0;  // bit i: parity of the next wait on ldb[i]
     uint32_t ld_pending = 0;  // bit i: a load into staging slab i not yet waited for
     int nbuf = 0;           // staging slab the next write goes to
@@ -655,6 +668,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long grow0 = static_cast<long long>(slot_base(g.d_m_base, tb, slot)) + rbase;
       const int gcol0 = slot_base(g.d_n_base, tb, slot) + tl.n0;
       const int ncols = min(pr.tile_n, N - tl.n0);
+      // this warp's column slabs [s_lo, s_hi): all of them, or with two warps
+      // per lane quarter the first or second half
+      int s_lo = 0, s_hi = ncols;
+      if constexpr (kEpiWarps == 8) {
+        const int per = ((ncols + SLAB - 1) / SLAB + 1) / 2 * SLAB;
+        s_lo = min(ncols, half * per);
+        s_hi = min(ncols, s_lo + per);
+      }
       // fetch an aux (pre-activation) slab into staging slab `b` (lane 0)
       auto fetch_aux = [&](int b, int s) {
         fence_proxy_async_smem();  // the lanes' reads of the slab precede the load
@@ -670,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
         nbuf = 0;
-        if (rows_ok > 0) fetch_aux(0, 0);  // overlaps the wait for the accumulator
+        if (rows_ok > 0 && s_lo < s_hi) fetch_aux(0, s_lo);  // overlaps the accumulator wait
       }
       if (!mbar_wait(&acc_full[buf], acc_phase, &abort_flag, wait_ns)) break;
       tc_fence_after();
@@ -711,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return p;
       };
 #pragma unroll 1
-      for (int s = 0; s < ncols && rows_ok > 0; s += SLAB) {
+      for (int s = s_lo; s < s_hi && rows_ok > 0; s += SLAB) {
         const int cvalid = min(SLAB, ncols - s);
         if constexpr (((CFG0 | CFG1) & kCfgSwiglu) != 0) if (epi == EPI_SWIGLU) {
           // gate accumulator columns at tbase + s, up columns tile_n further
@@ -764,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < SLAB; ++i) v[i] = 0.f;
         }
         if (dact) {
-          const int b = (s / SLAB) & 1;
+          const int b = ((s - s_lo) / SLAB) & 1;
           uint8_t* stg = stg_base + b * 4096;
           if (!mbar_wait(&ldb[b], (ld_phase >> b) & 1, &abort_flag, wait_ns)) {
             ok = false;
@@ -772,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ld_phase ^= 1u << b;
           ld_pending &= ~(1u << b);
-          if (s + SLAB < ncols) {
+          if (s + SLAB < s_hi) {
             // prefetch the next aux slab into the other staging slab (its
             // previous store, if any, must have finished reading it)
             if (lane == 0) bulk_wait_group_read<0>();
