@@ -482,7 +482,8 @@ def run_reference(args, cfg, name):
             "unavailable": (r.stderr.strip().splitlines() or ["no output"])[-1][:300]}
     except (subprocess.TimeoutExpired, OSError) as e:
         gpu = {"unavailable": str(e)[:300]}
-    procs = max(1, min(os.cpu_count() or 1, args.steps))
+    # one process per timed step, up to twice the cores: the timed steps run as one wave
+    procs = max(1, min(2 * (os.cpu_count() or 1), args.steps))
     cpu = time_reference_cpu(name, tokens, args.warmup, args.steps, procs)
     value = cpu["value"]
     sample = (f"{tokens} of the workload's {T} tokens per step: the reference's TritonMoEMLP "
@@ -505,7 +506,7 @@ def run_reference(args, cfg, name):
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) random-init weights)",
         "config": config_dict(name, cfg, ws),
         "execution": "host cores (the reference's Triton kernels under the Triton interpreter)",
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": procs, "kind": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": min(procs, os.cpu_count() or 1), "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
