@@ -473,7 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) MOE_TRACE_AT(1);
   // a pair's barriers are initialised before either CTA signals the other's
   if constexpr (CG == 2) cluster_sync();
-  tc_fence_after();
+  // the TMA producer (warp 0) issues no tcgen05 operation and does not read
+  // the TMEM address, so it starts its loads without this fence
+  if (warp != 0) tc_fence_after();
   if (threadIdx.x == 0) MOE_TRACE_AT(59);
   // The next kernel may start its own prologue now; it waits for this grid's
   // completion before touching memory.
@@ -532,6 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicExch(g.dep + g.dep_len + blk, 0);
           }
         }
+        if (ti == 0 && threadIdx.x == 0) MOE_TRACE_AT(62);
         if (tl.p == 0)
           ok = produce_tile<CFG0, T, CG>(ring, SB, S, full, empty, &abort_flag, wait_ns, &P.tmA[0],
                                          &P.tmB[0], nkb, am, ak, bn, bk, stage, phase, up_shift,

@@ -73,6 +73,17 @@ def main():
         end = us(tr[ctas, 2])
         print(f"== {n}: {len(ctas)} CTAs; after griddep wait {np.median(us(tr[ctas, 1])):.2f} us; "
               f"end median {np.median(end):.2f} max {end.max():.2f} us")
+        ntiles = np.array([sum(1 for i in range(8) if tr[c, 3 + 7 * i]) for c in ctas])
+        first_load = us(tr[ctas, 3])
+        print("  CTA end percentiles (10/25/50/75/90/100):",
+              " ".join(f"{np.percentile(end, q):.2f}" for q in (10, 25, 50, 75, 90, 100)),
+              f"| first tile's producer begin min {first_load.min():.2f} "
+              f"median {np.median(first_load):.2f}",
+              "| tiles per CTA:", dict(zip(*np.unique(ntiles, return_counts=True))))
+        marks = {s: tr[ctas, s] for s in (59, 60, 61, 62)}
+        print("  producer after the fence point / launch_dependents / table read / first tile decoded (median):",
+              " ".join(f"{np.median(us(v[v != 0])):.2f}" if (v != 0).any() else "-"
+                       for v in marks.values()))
         for i in range(4):
             cols = [3 + 7 * i + e for e in range(7)]
             sub = tr[ctas][:, cols]
