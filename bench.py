@@ -754,9 +754,9 @@ def run_ep_c5(args, dev, ws, rank, flush, peaks):
     """The expert-parallel config at this N: experts sharded over the ranks of
     the default group (N=1: a one-rank group, so the same exchange code path
     runs), every rank with its own 65536 tokens.  Timed eagerly (the exchange
-    sizes are read on the host once per step).  Parity: on a token slice every
-    rank compares the sharded layer's output and dX with the unsharded layer
-    (same weights, on this GPU)."""
+    plan is built on the host from the all-gathered counts once per forward).
+    Parity: on a token slice every rank compares the sharded layer's output
+    and dX with the unsharded layer (same weights, on this GPU)."""
     import torch
     import torch.distributed as dist
 
@@ -840,7 +840,7 @@ def run_ep_c5(args, dev, ws, rank, flush, peaks):
         "n_gpus": ws,
         "steps": steps,
         "parallelism": (f"experts sharded over {ws} GPU(s) ({'placed by measured router load' if args.placement == 'load' else 'round-robin'}), "
-                        f"NCCL all-to-all dispatch/combine, {T} tokens per GPU"),
+                        f"dispatch/combine over NVLink peer memory (NCCL barriers), {T} tokens per GPU"),
         "parity": parity,
         "roofline": {"bound": "tensor", "unit": "TFLOP/s", "peak": peaks[0],
                      "achieved_min_over_ranks": float(gflops.item()),

@@ -23,8 +23,9 @@ buffers.  Chunk c's transfers overlap the GEMMs of its neighbours: the
 dispatches of all chunks are queued first, each chunk's GEMMs wait only for
 its own rows, and each chunk's combine waits only for that chunk's GEMMs on
 every owner.  The GEMMs then run on fewer persistent CTAs (all SMs but
-`comm_sms`, 8 by default): a GEMM block holds nearly all of an SM's shared
-memory, so the exchange kernels need SMs of their own.  The per-(rank,
+`comm_sms`; by default 8 on two ranks and 16 on more, where most rows cross
+NVLink): a GEMM block holds nearly all of an SM's shared memory, so the
+exchange kernels need SMs of their own.  The per-(rank,
 chunk, expert) row counts are all-gathered and read on the host once per
 forward (the exchange plan); the backward reuses them.
 
@@ -530,7 +531,10 @@ class ExpertParallelMoEMLP(nn.Module):
         self._lb_coef_values = full._lb_coef_values
         self.chunks = max(1, int(chunks))
         if comm_sms is None:
-            comm_sms = int(os.environ.get("MOE_EP_COMM_SMS", "8"))
+            env = os.environ.get("MOE_EP_COMM_SMS")
+            # measured at 65536 tokens per GPU (c5): 8 best at 2 ranks; 16 at 4
+            # and 8 ranks, where 3/4 to 7/8 of the pulled rows cross NVLink
+            comm_sms = int(env) if env else (8 if self.world <= 2 else 16)
         self.comm_sms = max(0, int(comm_sms))
         self._comm: EPComm | None = None
         self._pool: list = []  # free owner-layout buffer sets (see _take_buffers)
