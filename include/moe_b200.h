@@ -288,8 +288,11 @@ MOE_API int moe_swiglu_grad(const void* grad_out, const void* gate, const void* 
  * per-block count in `dep`), so the down tiles fill the SMs the up tiles' tail
  * leaves idle instead of waiting for a second launch.  dep: an int32 device
  * buffer of at least moe_up_down_dep_words(rows, num_experts) words, zero
- * before the first call; each call returns it to zero.  Calls sharing a dep
- * buffer must not overlap. */
+ * before the first call; each call returns it to zero.  Calls on one GPU must
+ * not overlap at all (order them on one stream or with events): a down tile
+ * waits for other blocks' up tiles, so the whole grid has to be resident, and
+ * two overlapping launches could hold SMs against each other until their
+ * bounded waits give up (MOE_ERR_TIMEOUT). */
 MOE_API int64_t moe_up_down_dep_words(int64_t rows, int num_experts);
 MOE_API int moe_grouped_gemm_up_down(const void* x, int64_t rows, int64_t ld_x, const void* w1,
                                      const void* w2, int64_t hidden, int64_t total_width,

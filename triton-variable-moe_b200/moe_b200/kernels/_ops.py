@@ -431,8 +431,8 @@ _dep_buffers_retired: list = []
 
 def up_down_dep_buffer(device: torch.device, rows: int, num_experts: int) -> torch.Tensor:
     """Zeroed int32 row-block counters for gemm_up_down (every launch returns
-    them to zero); one per device, grown on demand, so gemm_up_down launches on
-    one device must not overlap (different streams without ordering)."""
+    them to zero); one per device, grown on demand.  gemm_up_down launches on
+    one device never overlap: see _order_up_down."""
     words = int(lib.moe_up_down_dep_words(rows, num_experts))
     device = torch.device(device)
     buf = _dep_buffers.get(device)
@@ -460,6 +460,27 @@ def reset_up_down_dep_buffer(device: torch.device) -> None:
         buf.zero_()
 
 
+_up_down_last_stream: dict = {}
+
+
+def _order_up_down(device: torch.device) -> None:
+    """Order this gemm_up_down launch after the device's previous one when that
+    ran on another stream.  The fused launch's down tiles wait for other CTAs'
+    up tiles, so its whole grid must be resident; two such grids overlapping on
+    unordered streams could hold SMs against each other (their waits would run
+    out, MOE_ERR_TIMEOUT), and they share the row-block counters.  One stream:
+    nothing is added.  While capturing a CUDA graph the capture's own ordering
+    applies (a wait on work outside the capture is not allowed)."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    cur = torch.cuda.current_stream(torch.device("cuda", idx))
+    prev = _up_down_last_stream.get(idx)
+    if prev is not None and prev.cuda_stream != cur.cuda_stream:
+        cur.wait_stream(prev)
+    _up_down_last_stream[idx] = cur
+
+
 def gemm_up_down(x, w1, w2, tok_off, w_off, tok_cnt, num_experts, inter, pre_act, out,
                  tile_n_width=0, tile_n_hidden=0):
     """inter = relu(x @ w1_e)^2 (pre_act = relu(x @ w1_e)), out = inter @ w2_e in
@@ -468,6 +489,7 @@ def gemm_up_down(x, w1, w2, tok_off, w_off, tok_cnt, num_experts, inter, pre_act
     tok_off, w_off, tok_cnt = _meta(tok_off), _meta(w_off), _meta(tok_cnt)
     H, TW = w1.shape
     dep = up_down_dep_buffer(x.device, x.shape[0], num_experts)
+    _order_up_down(x.device)
     ev = _ev_begin()
     rc = lib.moe_grouped_gemm_up_down(
         ptr(x), x.shape[0], x.stride(0), ptr(w1), ptr(w2), H, TW, ptr(tok_off), ptr(w_off),
