@@ -637,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int SLAB = 8 * EPC;      // columns per slab
     const int q = warp & 3;          // TMEM lane quarter (the hardware's warp % 4 rule)
     const int ew = warp - 2;         // epilogue warp index
-    const int half = ew / 4;         // with 8 warps: which half of the column slabs
+    [[maybe_unused]] const int half = ew / 4;  // with 8 warps: which half of the column slabs
     uint8_t* stg_base = sEpi + ew * 8192;
     uint64_t* ldb = epi_ld + ew * 2;
     uint32_t ld_phase = 0;  // bit i: parity of the next wait on ldb[i]
