@@ -517,12 +517,13 @@ def run_reference(args, cfg, name):
 
 
 # ------------------------------------------------------------------ our arm
-def capture_step(layer, x, gout, kernel_events=False):
+def capture_step(layer, x, gout, kernel_events=False, before_capture=None):
     """Capture one fwd+bwd of the layer in a CUDA graph (the layer never
     synchronises the host, so the whole step is capturable).  Returns the graph,
     its static output, how many of our kernels one replay launches and (with
     kernel_events) the (name, start, end) event pairs recorded around each of
-    our launches inside the graph."""
+    our launches inside the graph.  before_capture: called after the warm-up
+    steps, right before the capture."""
     import torch
 
     from moe_b200.kernels import _ops
@@ -538,6 +539,8 @@ def capture_step(layer, x, gout, kernel_events=False):
     torch.cuda.synchronize()
     layer.zero_grad(set_to_none=True)
     x.grad = None
+    if before_capture is not None:
+        before_capture()
     graph = torch.cuda.CUDAGraph()
     l0 = _ops.launch_count
     evs: list = []
@@ -556,16 +559,23 @@ GEMM_ENTRY_POINTS = ("moe_grouped_gemm_up_down", "moe_grouped_gemm_down_backward
                      "moe_grouped_gemm_up_backward")
 
 
-def capture_with_gemm_graph(layer, x, gout):
-    """capture_step, plus a second CUDA graph holding only the step's grouped-GEMM
+PERMUTE_ENTRY_POINTS = ("moe_padded_gather", "moe_padded_scatter")
+
+
+def capture_with_part_graphs(layer, x, gout):
+    """capture_step, plus one CUDA graph per group of launches (the step's
+    grouped-GEMM launches; its gather / combine launches), each holding those
     launches with the same arguments (the same buffers of the first graph's
-    memory pool), so that the GEMMs can be timed back to back without the
-    event-record nodes that break programmatic dependent launch."""
+    memory pool), so that they can be timed back to back without the
+    event-record nodes that break programmatic dependent launch.  Replaying a
+    part graph after the step graph rewrites the same values."""
     import torch
 
     from moe_b200 import _lib
 
-    orig = {n: getattr(_lib.lib, n) for n in GEMM_ENTRY_POINTS}
+    groups = {"gemm": GEMM_ENTRY_POINTS, "permute": PERMUTE_ENTRY_POINTS}
+    names = [n for g in groups.values() for n in g]
+    orig = {n: getattr(_lib.lib, n) for n in names}
     calls: list = []
 
     def wrap(n):
@@ -577,22 +587,25 @@ def capture_with_gemm_graph(layer, x, gout):
 
         return call
 
-    for n in GEMM_ENTRY_POINTS:
+    for n in names:
         setattr(_lib.lib, n, wrap(n))
     try:
-        graph, out, launches, _ = capture_step(layer, x, gout)
+        graph, out, launches, _ = capture_step(layer, x, gout, before_capture=calls.clear)
     finally:
-        for n in GEMM_ENTRY_POINTS:
+        for n in names:
             setattr(_lib.lib, n, orig[n])
-    step_calls = calls[-len(GEMM_ENTRY_POINTS):]  # the captured step's launches
-    gg = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gg, stream=torch.cuda.current_stream()):
-        st = torch.cuda.current_stream().cuda_stream
-        for n, a in step_calls:
-            rc = orig[n](*a[:-1], st)  # the stream is every entry point's last argument
-            if rc != 0:
-                raise RuntimeError(f"{n} failed in the GEMM-only graph: {rc}")
-    return graph, out, launches, gg, [n for n, _ in step_calls]
+    parts = {}
+    for key, entry in groups.items():
+        step_calls = [(n, a) for n, a in calls if n in entry]  # the captured step's launches
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg, stream=torch.cuda.current_stream()):
+            st = torch.cuda.current_stream().cuda_stream
+            for n, a in step_calls:
+                rc = orig[n](*a[:-1], st)  # the stream is every entry point's last argument
+                if rc != 0:
+                    raise RuntimeError(f"{n} failed in the {key}-only graph: {rc}")
+        parts[key] = (gg, [n for n, _ in step_calls])
+    return graph, out, launches, parts
 
 
 def timed_replays(fn, n, flush, ws=1, dist=None, dev=None) -> float:
@@ -688,22 +701,25 @@ def permute_roofline(pbytes, perm_ms, peak_hbm):
 
 def measure_single(name, cfg, dev, flush, steps, warmup, peaks):
     """A single-GPU config (c4) at its full size: graphed step tokens/s, the GEMM
-    roofline from a GEMM-only graph, the permutation roofline from per-kernel
-    events."""
+    roofline from a GEMM-only graph, the permutation roofline from a graph of the
+    gather / combine launches only."""
     import torch
 
     layer = build_layer(cfg, dev)
     x_h, g_h = make_tokens(cfg, 0)
     x = x_h.to(dev).requires_grad_(True)
     gout = g_h.to(dev)
-    graph, _out, _l, gg, names = capture_with_gemm_graph(layer, x, gout)
+    graph, _out, _l, parts = capture_with_part_graphs(layer, x, gout)
+    gg, names = parts["gemm"]
+    pg, _pnames = parts["permute"]
     for _ in range(max(warmup, 3)):
         graph.replay()
         gg.replay()
+        pg.replay()
     step_ms = timed_replays(graph.replay, steps, flush) / steps
     gemm_ms = timed_replays(gg.replay, steps, flush) / steps
+    perm_ms = timed_replays(pg.replay, steps, flush) / steps
     per_kind = kernel_times(layer, x, gout, flush)
-    perm_ms = sum(v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
     T = cfg["batch"] * cfg["seq"]
     flops = gemm_flops(routed_counts(layer, x, cfg["top_k"]).cpu().tolist(), cfg)
     out = {
@@ -714,10 +730,13 @@ def measure_single(name, cfg, dev, flush, steps, warmup, peaks):
         "roofline": gemm_roofline(flops, gemm_ms, len(names), names, peaks[0], peaks[2],
                                   how="CUDA graph of the step's GEMM launches only, L2 flushed "
                                       "before each replay"),
-        "permute_roofline": permute_roofline(permute_bytes(cfg), perm_ms, peaks[1]),
+        "permute_roofline": dict(
+            permute_roofline(permute_bytes(cfg), perm_ms, peaks[1]),
+            timing="CUDA graph of the step's gather / combine launches only, L2 flushed "
+                   "before each replay"),
         "kernel_us_per_step": {k: round(v * 1e3, 2) for k, v in sorted(per_kind.items())},
     }
-    del graph, gg, layer
+    del graph, gg, pg, layer
     torch.cuda.empty_cache()
     return out
 
@@ -940,11 +959,13 @@ def run_b200(args, cfg, name):
         dist.destroy_process_group()
         return 0
 
-    graph, out_static, per_step_launches, gemm_graph, gemm_names = capture_with_gemm_graph(
-        layer, x, gout)
+    graph, out_static, per_step_launches, parts = capture_with_part_graphs(layer, x, gout)
+    gemm_graph, gemm_names = parts["gemm"]
+    perm_graph, perm_names = parts["permute"]
     for _ in range(3):
         graph.replay()
         gemm_graph.replay()
+        perm_graph.replay()
     torch.cuda.synchronize()
 
     # clock samples: a ~1.5 s soak of the same step right before the timed loop
@@ -970,8 +991,14 @@ def run_b200(args, cfg, name):
                              how="CUDA graph of the step's GEMM launches only (same buffers), "
                                  "L2 flushed before each replay")
     per_kind = kernel_times(layer, x, gout, flush)
-    perm_ms = sum(v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
+    # the gather / combine launches alone, back to back (as for the GEMMs)
+    perm_ms = timed_replays(perm_graph.replay, args.steps, flush) / args.steps
     permute = permute_roofline(permute_bytes(cfg), perm_ms, peaks[1])
+    permute["kernels"] += f" ({', '.join(perm_names)})"
+    permute["timing"] = ("CUDA graph of the step's gather / combine launches only (same "
+                         "buffers), L2 flushed before each replay")
+    permute["ms_per_step_event_timed"] = sum(
+        v for k, v in per_kind.items() if k in ("gather", "weighted_gather", "combine"))
     kernel_us = {k: round(v * 1e3, 2) for k, v in sorted(per_kind.items())}
 
     # End to end through the public API with host buffers.  Every step copies its
@@ -1052,7 +1079,7 @@ def run_b200(args, cfg, name):
     e2e_ok = bool(torch.equal(out_host[(args.steps - 1) % 2],
                               slots[(args.steps - 1) % 2][3].detach().cpu()))
     nbytes = x_host.numel() * 2
-    del slots, graph, graph2, gemm_graph, layer, out_static, out2, x, x2, gout, g2
+    del slots, graph, graph2, gemm_graph, perm_graph, layer, out_static, out2, x, x2, gout, g2
     torch.cuda.empty_cache()
 
     extra = {}
