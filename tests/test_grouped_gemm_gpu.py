@@ -286,3 +286,74 @@ def test_fused_up_down_matches_separate_launches(case, tiles, device):
         assert torch.equal(y, y2)
         dep = _ops.up_down_dep_buffer(device, m["rows"], m["E"])
         assert int(dep.abs().sum().item()) == 0
+
+
+SKEWED = ([256] * 8, [2000, 700, 300, 100, 40, 10, 0, 5], 512, 64)
+
+
+@pytest.mark.parametrize("ctas", [3, 7])
+def test_ticket_schedule_backward_matches_round_robin(ctas, device):
+    """With at least 8 tiles per CTA a launch takes its tiles by ticket from a
+    per-stream counter (skewed routing makes the weight-gradient tiles' K very
+    unequal).  Capping the grid forces that schedule at a small size; every
+    output equals the round-robin launch of the full grid bit for bit, the
+    counter is reused across launches, and dW1 matches the fp32 reference."""
+    from moe_b200 import _lib
+    from moe_b200.kernels import _ops
+
+    widths, counts, H, bs = SKEWED
+    t, m = make_problem(widths, counts, H, bs, device=device, seed=21)
+    args = (m["tok_off"], m["w_off"], m["tpe"], m["E"])
+    cap = _lib.tile_ctas(ctas)
+
+    def run(extra):
+        dact = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
+        gw2 = torch.full((m["TW"], H), 7.0, dtype=torch.bfloat16, device=device)
+        _ops.gemm_down_backward(t["gy"], t["ga"], t["w2"], *args, dact, gw2,
+                                pre_act=t["pre"], tile_n_width=128 | extra,
+                                tile_n_hidden=256 | extra)
+        gx = torch.zeros(m["rows"], H, dtype=torch.bfloat16, device=device)
+        gw1 = torch.full((H, m["TW"]), 7.0, dtype=torch.bfloat16, device=device)
+        _ops.gemm_up_backward(t["ga"], t["x"], t["w1"], *args, gx, gw1,
+                              tile_n_width=128 | extra, tile_n_hidden=256 | extra)
+        torch.cuda.synchronize()
+        _ops.check_device_status(device)
+        return dact, gw2, gx, gw1
+
+    want = run(0)
+    for _rep in range(3):  # the ticket counter returns to zero after every launch
+        for a, b in zip(run(cap), want):
+            assert torch.equal(a, b)
+    gw1 = want[3]
+    for e in range(m["E"]):
+        r0, r1, c0, c1 = m["tok"][e], m["tok"][e + 1], m["wo"][e], m["wo"][e + 1]
+        ref = t["x"][r0:r1].float().T @ t["ga"][r0:r1, : c1 - c0].float()
+        assert_close(gw1[:, c0:c1], ref, f"gw1 e{e}")
+
+
+@pytest.mark.parametrize("ctas", [2, 5])
+def test_ticket_schedule_fused_forward(ctas, device):
+    """The fused up + down launch on a capped grid takes its tiles by ticket:
+    every up tile is taken before any down tile, so a down tile waits only for
+    up tiles that running blocks hold.  Same results as the separate launches."""
+    from moe_b200 import _lib
+    from moe_b200.kernels import _ops
+
+    widths, counts, H, bs = SKEWED
+    t, m = make_problem(widths, counts, H, bs, device=device, seed=22)
+    args = (m["tok_off"], m["w_off"], m["tpe"], m["E"])
+    cap = _lib.tile_ctas(ctas)
+    h2 = torch.zeros(m["rows"], m["maxw"], dtype=torch.bfloat16, device=device)
+    pre2 = torch.zeros_like(h2)
+    _ops.gemm_up(t["x"], t["w1"], *args, "relu_squared", h2, pre2, tile_n=256)
+    y2 = torch.zeros(m["rows"], H, dtype=torch.bfloat16, device=device)
+    _ops.gemm_down(h2, t["w2"], *args, y2, tile_n=256)
+    for _rep in range(2):
+        h = torch.zeros_like(h2)
+        pre = torch.zeros_like(h2)
+        y = torch.zeros_like(y2)
+        _ops.gemm_up_down(t["x"], t["w1"], t["w2"], *args, h, pre, y, tile_n_width=256 | cap,
+                          tile_n_hidden=256 | cap)
+        torch.cuda.synchronize()
+        _ops.check_device_status(device)
+        assert torch.equal(h, h2) and torch.equal(pre, pre2) and torch.equal(y, y2)

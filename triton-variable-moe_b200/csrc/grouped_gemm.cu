@@ -18,7 +18,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 #include <type_traits>
 
 #include "grouped_gemm.cuh"
@@ -47,7 +49,9 @@ constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-bl
 constexpr int kSmemMax = 227 * 1024;     // dynamic shared memory per CTA on sm_100
 constexpr int kEpiBytes = kEpiWarps * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
-constexpr int kBarBytes = 512;            // mbarriers, TMEM address, abort flag
+constexpr int kBarBytes = 640;            // mbarriers, TMEM address, abort flag, tile queue
+constexpr int kTileQ = 8;                 // tile queue entries (producer -> MMA / epilogue)
+constexpr int kDynMinTiles = 8;           // tiles per unit from which tiles are taken by ticket
 
 struct Problem {
   GroupedGemmDesc g;
@@ -68,6 +72,7 @@ struct MultiParams {
   int stage_bytes;  // A tile + largest B tile
   int smem_bytes;   // dynamic shared memory of the launch
   unsigned long long wait_ns;  // limit of every device-side wait (ns)
+  int* sched;  // tile-ticket counter (zero between launches), or null: round-robin tiles
 };
 
 // Per (problem, expert) slot: tile prefix, extents and the two offsets every
@@ -350,6 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
   int& abort_flag = *reinterpret_cast<int*>(bars + 2 * kMaxStages + 14);
   uint64_t* peer_full = bars + 2 * kMaxStages + 15;  // [stages], even CTA of a pair
+  // tile queue: the producer pushes each tile's index (-1 after the last);
+  // the MMA issuer (or a pair's relay) and every epilogue warp pop it
+  uint64_t* tq_full = bars + 3 * kMaxStages + 15 + 2 * 8;  // after epi_ld's 16 slots
+  uint64_t* tq_empty = tq_full + kTileQ;
+  int* tq = reinterpret_cast<int*>(tq_empty + kTileQ);
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   const int unit = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
   const int nunits = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
@@ -385,6 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&epi_ld[i], 1);
+    for (int i = 0; i < kTileQ; ++i) {
+      mbar_init(&tq_full[i], 1);
+      mbar_init(&tq_empty[i], 1 + kEpiWarps);
+    }
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -484,6 +498,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int total = tb.prefix[nge];
   if (threadIdx.x == 0 && total >= 0) MOE_TRACE_AT(61);
+  // Tile order: round-robin (unit, unit + nunits, ...), or, with many tiles per
+  // unit, by ticket from a global counter: each unit's producer takes the next
+  // tile when it starts one, so the units that hold long tiles (the weight
+  // gradients of popular experts, K = their token count) take fewer, while
+  // the tiles in flight stay neighbours (their A and B tiles shared in L2).
+  // Tickets come in order, so a down tile of the fused forward only ever
+  // waits for up tiles that running units hold.
+  const bool dyn = CG == 1 && P.sched != nullptr && total >= kDynMinTiles * nunits;
+  // a consumer's next tile from the queue (-1: no more, -2: gave up waiting);
+  // `leader` releases the entry for the consumer (one arrival per consumer)
+  auto pop = [&](int& qi, uint32_t& qph, bool leader) -> int {
+    if (!mbar_wait(&tq_full[qi], qph, &abort_flag, wait_ns)) return -2;
+    const int v = tq[qi];
+    __syncwarp(__activemask());
+    if (leader) mbar_arrive(&tq_empty[qi]);
+    if (++qi == kTileQ) {
+      qi = 0;
+      qph ^= 1;
+    }
+    return v;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -492,7 +527,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int ti = 0, issued = 0;
-      for (int t = unit; t < total && ok; t += nunits, ++ti) {
+      int qi = 0;
+      uint32_t qph = 0;
+      auto push = [&](int v) -> bool {  // publish the next tile to the consumers
+        if (!mbar_wait(&tq_empty[qi], qph ^ 1, &abort_flag, wait_ns)) return false;
+        tq[qi] = v;
+        mbar_arrive(&tq_full[qi]);  // release: the index is visible with the phase
+        if (++qi == kTileQ) {
+          qi = 0;
+          qph ^= 1;
+        }
+        return true;
+      };
+      int t = dyn ? atomicAdd(P.sched, 1) : unit;
+      for (; t < total && ok; ++ti) {
+        if (!push(t)) {
+          ok = false;
+          break;
+        }
+        // the next tile, taken now so that the ticket's round trip overlaps
+        // this tile's loads
+        const int t_next = dyn ? atomicAdd(P.sched, 1) : t + nunits;
         MOE_TRACE_TILE(ti, 0);
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const Problem& pr = P.pr[tl.p];
@@ -544,6 +599,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          &P.tmB[1], nkb, am, ak, bn, bk, stage, phase, up_shift,
                                          issued);
         MOE_TRACE_TILE(ti, 2);
+        t = t_next;
+      }
+      if (ok) ok = push(-1);  // no more tiles
+      if (dyn) {
+        // every unit ends with one ticket past the last tile (after an abort it
+        // takes the rest first); the holder of the last ticket issued returns
+        // the counter to zero for the next launch on this stream
+        while (t < total) t = atomicAdd(P.sched, 1);
+        if (t == total + nunits - 1) atomicExch(P.sched, 0);
       }
       if (!ok) drain_loads(full, S, stage, phase, issued, wait_ns);
     }
@@ -557,7 +621,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       int ti = 0, seen = 0;
-      for (int t = unit; t < total && ok; t += nunits, ++ti) {
+      int qi = 0;
+      uint32_t qph = 0;
+      for (;; ++ti) {
+        const int t = pop(qi, qph, true);
+        if (t < 0) break;
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int K = tb.K[tl.slot];
         const int nkb = (K + Elem<T>::BKE - 1) / Elem<T>::BKE;
@@ -599,7 +667,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, seen = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += nunits) {
+      int qi = 0;
+      uint32_t qph = 0;
+      while (ok) {
+        const int t = pop(qi, qph, true);
+        if (t < 0) break;
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int nkb = (tb.K[tl.slot] + Elem<T>::BKE - 1) / Elem<T>::BKE;
         for (int kb = 0; kb < nkb; ++kb) {
@@ -652,7 +724,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     bool ok = true;
     int ti = 0;
-    for (int t = unit; t < total && ok; t += nunits, ++ti) {
+    int qi = 0;
+    uint32_t qph = 0;
+    for (; ok; ++ti) {
+      const int t = pop(qi, qph, lane == 0);
+      if (t < 0) break;
       const Tile tl = decode_tile<BMT>(tb, P, nge, t);
       const Problem& pr = P.pr[tl.p];
       const GroupedGemmDesc& g = pr.g;
@@ -1069,6 +1145,43 @@ int dispatch_dtype(int dtype, int cg, int used, int c0, int c1, const MultiParam
   return dispatch<__nv_bfloat16, 1>(used, c0, c1, P, grid, st);
 }
 
+// Tile-ticket counter of the launches on one (device, stream): zero between
+// launches (each launch's last ticket holder returns it to zero), so launches
+// that are ordered on one stream share it and launches on different streams
+// never do.  Allocated (and zeroed on that stream) at the first launch outside
+// stream capture; a stream that is capturing and has none yet gets null, and
+// its launches take round-robin tiles.  A graph captured with a counter keeps
+// it: its replays must not overlap launches on the capturing stream.
+// (cudaStreamPerThread is one handle for all host threads: launches on it
+// from several threads at once would share a counter.)
+int* sched_counter(cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, int*> counters;
+  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
+  std::lock_guard<std::mutex> lock(mu);
+  const auto it = counters.find(key);
+  if (it != counters.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  int* p = nullptr;
+  if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemsetAsync(p, 0, sizeof(int), st) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return nullptr;
+  }
+  counters[key] = p;
+  return p;
+}
+
 int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const int* epis, int n,
                       int dtype, cudaStream_t st) {
   if (n <= 0 || n > kMaxProblems) return kStatusBadArg;
@@ -1138,6 +1251,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   P.nprob = used;
   if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0 || grid > num_sms()) grid = num_sms();
+  P.sched = cg == 1 ? sched_counter(st) : nullptr;
 #ifdef MOE_TRACE
   if (const char* g = getenv("MOE_TRACE_GRID")) grid = atoi(g);  // timeline experiments only
 #endif
