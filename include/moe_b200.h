@@ -51,6 +51,14 @@ extern "C" {
 /* tile_n field: run the launch on at most n persistent CTAs (0 = one per SM),
  * e.g. to leave SMs to communication kernels running alongside */
 #define MOE_TILE_CTAS(n) ((n) << 16)
+/* Grouped-GEMM tile order: a launch with at least 8 tiles per CTA takes its
+ * tiles by ticket from a counter the library keeps per (device, stream) --
+ * allocated at the first such call on that stream outside graph capture and
+ * zero again after every launch -- so launches ordered on one stream share it
+ * and launches on different streams never do.  A graph captured on a stream
+ * uses that stream's counter: replay it where it cannot overlap other
+ * launches of that stream.  Fewer tiles, CTA pairs, or capture on a stream
+ * without a counter: round-robin tiles. */
 
 #define MOE_ACT_NONE 0
 #define MOE_ACT_RELU_SQUARED 1
