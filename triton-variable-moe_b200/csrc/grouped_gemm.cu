@@ -334,7 +334,7 @@ __device__ __forceinline__ bool mma_tile(uint8_t* ring, int SB, int S, uint64_t*
 // CG = 2: launched as 2-CTA clusters; the pair computes 256-row tiles with
 // cta_group::2 MMAs issued by the even CTA, each CTA holding its 128 rows of
 // the accumulator and running its own producer and epilogue.
-template <typename T, int CFG0, int CFG1, int CG>
+template <typename T, int CFG0, int CFG1, int CG, bool DYN>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ MultiParams P) {
   constexpr int BMT = BM * CG;  // tile rows
@@ -355,8 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
   int& abort_flag = *reinterpret_cast<int*>(bars + 2 * kMaxStages + 14);
   uint64_t* peer_full = bars + 2 * kMaxStages + 15;  // [stages], even CTA of a pair
-  // tile queue: the producer pushes each tile's index (-1 after the last);
-  // the MMA issuer (or a pair's relay) and every epilogue warp pop it
+  // tile queue (ticket order only): the producer pushes each tile's index (-1
+  // after the last); the MMA issuer (or a pair's relay) and every epilogue
+  // warp pop it
   uint64_t* tq_full = bars + 3 * kMaxStages + 15 + 2 * 8;  // after epi_ld's 16 slots
   uint64_t* tq_empty = tq_full + kTileQ;
   int* tq = reinterpret_cast<int*>(tq_empty + kTileQ);
@@ -395,9 +396,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&epi_ld[i], 1);
-    for (int i = 0; i < kTileQ; ++i) {
-      mbar_init(&tq_full[i], 1);
-      mbar_init(&tq_empty[i], 1 + kEpiWarps);
+    if constexpr (DYN) {
+      for (int i = 0; i < kTileQ; ++i) {
+        mbar_init(&tq_full[i], 1);
+        mbar_init(&tq_empty[i], 1 + kEpiWarps);
+      }
     }
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -505,10 +508,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the tiles in flight stay neighbours (their A and B tiles shared in L2).
   // Tickets come in order, so a down tile of the fused forward only ever
   // waits for up tiles that running units hold.
-  const bool dyn = CG == 1 && P.sched != nullptr && total >= kDynMinTiles * nunits;
-  // a consumer's next tile from the queue (-1: no more, -2: gave up waiting);
-  // `leader` releases the entry for the consumer (one arrival per consumer)
-  auto pop = [&](int& qi, uint32_t& qph, bool leader) -> int {
+  // (DYN: the kernel built with the ticket path; the round-robin build has
+  // none of the queue code)
+  const bool dyn = DYN && CG == 1 && P.sched != nullptr && total >= kDynMinTiles * nunits;
+  // A consumer's next tile (-1: no more, -2: gave up waiting): round-robin
+  // tiles are computed in place (`rr` starts at unit - nunits); ticket tiles
+  // come from the queue, where `leader` releases the entry for the consumer
+  // (one arrival per consumer).
+  auto pop = [&](int& rr, int& qi, uint32_t& qph, bool leader) -> int {
+    if (!dyn) {
+      rr += nunits;
+      return rr < total ? rr : -1;
+    }
     if (!mbar_wait(&tq_full[qi], qph, &abort_flag, wait_ns)) return -2;
     const int v = tq[qi];
     __syncwarp(__activemask());
@@ -541,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int t = dyn ? atomicAdd(P.sched, 1) : unit;
       for (; t < total && ok; ++ti) {
-        if (!push(t)) {
+        if (dyn && !push(t)) {
           ok = false;
           break;
         }
@@ -601,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         MOE_TRACE_TILE(ti, 2);
         t = t_next;
       }
-      if (ok) ok = push(-1);  // no more tiles
+      if (dyn && ok) ok = push(-1);  // no more tiles
       if (dyn) {
         // every unit ends with one ticket past the last tile (after an abort it
         // takes the rest first); the holder of the last ticket issued returns
@@ -621,10 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       int ti = 0, seen = 0;
-      int qi = 0;
+      int qi = 0, rr = unit - nunits;
       uint32_t qph = 0;
       for (;; ++ti) {
-        const int t = pop(qi, qph, true);
+        const int t = pop(rr, qi, qph, true);
         if (t < 0) break;
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int K = tb.K[tl.slot];
@@ -667,10 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, seen = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int qi = 0;
+      int qi = 0, rr = unit - nunits;
       uint32_t qph = 0;
       while (ok) {
-        const int t = pop(qi, qph, true);
+        const int t = pop(rr, qi, qph, true);
         if (t < 0) break;
         const Tile tl = decode_tile<BMT>(tb, P, nge, t);
         const int nkb = (tb.K[tl.slot] + Elem<T>::BKE - 1) / Elem<T>::BKE;
@@ -724,10 +735,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     bool ok = true;
     int ti = 0;
-    int qi = 0;
+    int qi = 0, rr = unit - nunits;
     uint32_t qph = 0;
     for (; ok; ++ti) {
-      const int t = pop(qi, qph, lane == 0);
+      const int t = pop(rr, qi, qph, lane == 0);
       if (t < 0) break;
       const Tile tl = decode_tile<BMT>(tb, P, nge, t);
       const Problem& pr = P.pr[tl.p];
@@ -999,9 +1010,9 @@ int make_tmap(CUtensorMap* tm, const void* base, int dtype, long long inner, lon
   return r == CUDA_SUCCESS ? kStatusOk : kStatusBadArg;
 }
 
-template <typename T, int C0, int C1, int CG>
-int launch(const MultiParams& P, int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<T, C0, C1, CG>;
+template <typename T, int C0, int C1, int CG, bool DYN>
+int launch_kernel(const MultiParams& P, int grid, cudaStream_t st) {
+  auto kern = grouped_gemm_kernel<T, C0, C1, CG, DYN>;
   static bool attr_set[64] = {};   // per device
   static int max_pairs[64] = {};   // co-resident 2-CTA clusters, per device
   static std::mutex attr_mu;       // callers may be on several host threads
@@ -1048,6 +1059,15 @@ int launch(const MultiParams& P, int grid, cudaStream_t st) {
   cfg.gridDim = dim3(grid);
   if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return kStatusCuda;
   return cudaPeekAtLastError() == cudaSuccess ? kStatusOk : kStatusCuda;
+}
+
+// The ticket-order build when the host gave the launch a counter (single
+// CTAs, many tiles expected), else the round-robin build.
+template <typename T, int C0, int C1, int CG>
+int launch(const MultiParams& P, int grid, cudaStream_t st) {
+  if constexpr (CG == 1)
+    if (P.sched != nullptr) return launch_kernel<T, C0, C1, CG, true>(P, grid, st);
+  return launch_kernel<T, C0, C1, CG, false>(P, grid, st);
 }
 
 // One problem: any of the 8 operand configurations.
@@ -1251,7 +1271,23 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   P.nprob = used;
   if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0 || grid > num_sms()) grid = num_sms();
-  P.sched = cg == 1 ? sched_counter(st) : nullptr;
+  // ticket-ordered tiles only where many tiles per CTA are expected (upper
+  // estimate from the operands' extents; the kernel checks the real count)
+  long long est = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmOperands& op = ops[i];
+    const GroupedGemmDesc& g = gs[i];
+    if (g.E <= 0) continue;
+    const long long bn = op.bn == 256 ? 256 : 128;
+    const long long m_ext = op.a_mn ? op.a_cols : op.a_rows;
+    const long long n_ext = op.b_mn ? op.b_cols : op.b_rows;
+    const long long m_blocks = (m_ext + BM - 1) / BM;
+    const long long mb = g.m_src == DIM_CONST ? g.E * m_blocks : m_blocks;
+    const long long n_per_expert = g.n_src == DIM_CONST ? n_ext : (n_ext + g.E - 1) / g.E;
+    est += mb * ((n_per_expert + bn - 1) / bn);
+  }
+  P.sched = (cg == 1 && est >= static_cast<long long>(kDynMinTiles) * grid) ? sched_counter(st)
+                                                                            : nullptr;
 #ifdef MOE_TRACE
   if (const char* g = getenv("MOE_TRACE_GRID")) grid = atoi(g);  // timeline experiments only
 #endif
