@@ -47,7 +47,12 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxStages = 8;
 constexpr int kABytes = BM * 128;        // 16 KB: 128 rows of one 128-byte k-block
 constexpr int kSmemMax = 227 * 1024;     // dynamic shared memory per CTA on sm_100
-constexpr int kEpiBytes = kEpiWarps * 2 * 32 * 128;  // per epilogue warp: two 32-row x 128-byte slabs
+// Epilogue staging per warp: two 32-row x 128-byte slabs (a slab is rewritten
+// while the other's TMA store reads it), or one in the ticket-order build,
+// whose long tiles leave the epilogue time to spare and which needs the 16 KB
+// for its ring (4 stages of 48 KB beside a large slot table).
+constexpr int epi_slabs(bool dyn) { return dyn ? 1 : 2; }
+constexpr int epi_bytes(bool dyn) { return kEpiWarps * epi_slabs(dyn) * 32 * 128; }
 constexpr int kTmemCols = 2 * BN_MAX;    // double-buffered fp32 accumulator
 constexpr int kBarBytes = 640;            // mbarriers, TMEM address, abort flag, tile queue
 constexpr int kTileQ = 8;                 // tile queue entries (producer -> MMA / epilogue)
@@ -344,8 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = P.stages;
   const int SB = P.stage_bytes;
   uint8_t* ring = smem;                // stage s: A at s*SB, B at s*SB + kABytes
-  uint8_t* sEpi = smem + S * SB;       // epilogue staging, 8 KB per warp
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
+  uint8_t* sEpi = smem + S * SB;       // epilogue staging, 4 KB slabs per warp
+  constexpr int kSlabs = epi_slabs(DYN);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + epi_bytes(DYN));
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   uint64_t* acc_full = bars + 2 * kMaxStages;
@@ -710,8 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every lane converts its own row into a shared staging slab laid out in
     // the TMA 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)), then
     // one lane stores the slab with a TMA tensor store and the warp moves on;
-    // two staging slabs per warp alternate, so a slab is rewritten only after
-    // its previous store has finished reading it.  Slabs that straddle an
+    // two staging slabs per warp alternate (one slab in the ticket-order
+    // build), so a slab is rewritten only after its previous store has
+    // finished reading it.  Slabs that straddle an
     // expert's last row or column are stored by the lanes instead (row-major,
     // four 128-byte rows per instruction), never past the expert's extent.
     // The relu^2-derivative epilogue fetches its pre-activation slab by TMA
@@ -721,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;          // TMEM lane quarter (the hardware's warp % 4 rule)
     const int ew = warp - 2;         // epilogue warp index
     [[maybe_unused]] const int half = ew / 4;  // with 8 warps: which half of the column slabs
-    uint8_t* stg_base = sEpi + ew * 8192;
+    uint8_t* stg_base = sEpi + ew * (kSlabs * 4096);
     uint64_t* ldb = epi_ld + ew * 2;
     uint32_t ld_phase = 0;  // bit i: parity of the next wait on ldb[i]
     uint32_t ld_pending = 0;  // bit i: a load into staging slab i not yet waited for
@@ -815,10 +822,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // the next staging slab, once its previous TMA store has read it
       auto next_stage = [&]() -> uint8_t* {
-        if (lane == 0) bulk_wait_group_read<1>();
+        if (lane == 0) bulk_wait_group_read<kSlabs - 1>();
         __syncwarp();
         uint8_t* p = stg_base + nbuf * 4096;
-        nbuf ^= 1;
+        if constexpr (kSlabs == 2) nbuf ^= 1;
         return p;
       };
 #pragma unroll 1
@@ -875,15 +882,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < SLAB; ++i) v[i] = 0.f;
         }
         if (dact) {
-          const int b = ((s - s_lo) / SLAB) & 1;
+          const int b = kSlabs == 2 ? ((s - s_lo) / SLAB) & 1 : 0;
           uint8_t* stg = stg_base + b * 4096;
+          if (kSlabs == 1 && s != s_lo) {
+            // one slab: this slab's pre-activation once the previous store has
+            // read the slab
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            fetch_aux(0, s);
+          }
           if (!mbar_wait(&ldb[b], (ld_phase >> b) & 1, &abort_flag, wait_ns)) {
             ok = false;
             break;
           }
           ld_phase ^= 1u << b;
           ld_pending &= ~(1u << b);
-          if (s + SLAB < s_hi) {
+          if (kSlabs == 2 && s + SLAB < s_hi) {
             // prefetch the next aux slab into the other staging slab (its
             // previous store, if any, must have finished reading it)
             if (lane == 0) bulk_wait_group_read<0>();
@@ -902,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *chunk_at(stg, lane, j) = pack_chunk<T>(o);
           }
           put(stg, tmD, D, g.ldd, s, cvalid);
-          nbuf = b ^ 1;  // the other slab is the older one now
+          nbuf = kSlabs == 2 ? b ^ 1 : 0;  // the other slab is the older one now
         } else {
           if (epi == EPI_RELU2) {
 #pragma unroll
@@ -1138,7 +1152,9 @@ int num_sms() {
 static bool plan_smem(MultiParams& P, int bn_max, int cg) {
   const int nge = P.pr[0].g.E + (P.nprob > 1 ? P.pr[1].g.E : 0);
   P.stage_bytes = kABytes + bn_max / cg * 128;
-  const int fixed = 1024 + kEpiBytes + kBarBytes + table_bytes(nge);
+  // the ticket-order build (a counter given, single CTAs) stages one slab per warp
+  const bool dyn = cg == 1 && P.sched != nullptr;
+  const int fixed = 1024 + epi_bytes(dyn) + kBarBytes + table_bytes(nge);
   int stages = (kSmemMax - fixed) / P.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
@@ -1269,7 +1285,6 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   }
   if (used == 0) return kStatusOk;
   P.nprob = used;
-  if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
   if (grid <= 0 || grid > num_sms()) grid = num_sms();
   // ticket-ordered tiles only where many tiles per CTA are expected (upper
   // estimate from the operands' extents; the kernel checks the real count)
@@ -1288,6 +1303,7 @@ int run_grouped_gemms(const GemmOperands* ops, const GroupedGemmDesc* gs, const 
   }
   P.sched = (cg == 1 && est >= static_cast<long long>(kDynMinTiles) * grid) ? sched_counter(st)
                                                                             : nullptr;
+  if (!plan_smem(P, bn_max, cg)) return kStatusUnsupported;
 #ifdef MOE_TRACE
   if (const char* g = getenv("MOE_TRACE_GRID")) grid = atoi(g);  // timeline experiments only
 #endif
